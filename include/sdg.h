@@ -1,0 +1,172 @@
+/* sdg.h — C ABI of the B200 SD1.5 UNet engine (libsdg.so).
+ *
+ * Drop-in for the JNI surface of the reference's Vulkan engine
+ * (Shoolife/sd-vulkan-pixel10-tensor-g5, app/src/main/cpp/vk_engine.cpp and
+ * app/src/main/java/.../sd/VulkanBench.kt:10-27). Every entry point returns an
+ * int status (SDG_OK == 0); sdg_last_error() gives the message of the last
+ * failure on the calling thread.
+ *
+ * Conventions
+ *   - Host arrays are caller-owned and copied in/out within the call.
+ *   - "Device" pointers are CUDA device pointers on the engine's device.
+ *   - Activations in the op surface are fp16 NHWC (== token-major [B*H*W, C]).
+ *   - Weights handed to sdg_upload_weight use the reference's on-disk format:
+ *     one raw fp16 array per diffusers state-dict key; conv [Co,Ci,kh,kw];
+ *     norm [C]; every Linear weight TRANSPOSED [in,out] (vk_engine.cpp:497-507).
+ *   - One engine per GPU; calls on one engine must be serialised (the
+ *     reference serialises on one GpuThread, GenerateViewModel.kt:31).
+ */
+#ifndef SDG_H_
+#define SDG_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SDG_API __attribute__((visibility("default")))
+
+enum {
+  SDG_OK = 0,
+  SDG_ERR_CUDA = 1,           /* CUDA runtime / launch error */
+  SDG_ERR_ARG = 2,            /* bad argument (null, size) */
+  SDG_ERR_SHAPE = 3,          /* unsupported shape */
+  SDG_ERR_MISSING_WEIGHT = 4, /* a UNet key was never uploaded */
+  SDG_ERR_TIMEOUT = 5,        /* host-side wait deadline expired */
+  SDG_ERR_IO = 6,             /* weight file missing / short */
+  SDG_ERR_NOT_INIT = 7,       /* null or released engine */
+  SDG_ERR_DEVICE = 8,         /* a kernel's bounded wait expired (device error word set) */
+  SDG_ERR_NCCL = 9,           /* collective failure (multi-GPU gather) */
+  SDG_ERR_UNSUPPORTED = 10
+};
+
+typedef struct sdg_engine sdg_engine;
+
+typedef struct sdg_profile_row {
+  char name[32];   /* op category: GN, LN, CONV3, GEMM, ATTN, GEMV, MISC */
+  double ms;       /* summed device time of that category in one forward */
+  int launches;
+} sdg_profile_row;
+
+/* --- lifecycle --------------------------------------------------------------- */
+
+/* Replaces Java_..._unetInit(shaders, dir) (vk_engine.cpp:796-808): create an
+ * engine on CUDA device `device`. When `weights_dir` is non-null every UNet key
+ * is read from <weights_dir>/<key>.bin (the reference loads them lazily at
+ * vk_engine.cpp:497-507; here they are read once, here). */
+SDG_API int sdg_init(int device, const char* weights_dir, sdg_engine** out);
+
+/* One weight in the reference format (see above). `shape` is the PyTorch
+ * shape (ndim entries) used to validate the byte count. Replaces the file read
+ * inside W(name) (vk_engine.cpp:497-507). */
+SDG_API int sdg_upload_weight(sdg_engine* e, const char* key, const uint16_t* fp16, const int64_t* shape, int ndim);
+
+/* Read every UNet key from <dir>/<key>.bin (reference directory format). */
+SDG_API int sdg_load_dir(sdg_engine* e, const char* dir);
+
+/* Build device layouts from the uploaded weights (implicit on first forward).
+ * Returns SDG_ERR_MISSING_WEIGHT naming the first absent key. */
+SDG_API int sdg_prepare(sdg_engine* e);
+
+/* Replaces Java_..._unetRelease (vk_engine.cpp:915-926): frees everything. */
+SDG_API int sdg_release(sdg_engine* e);
+
+/* Message of the last failing call on this thread (empty when none). */
+SDG_API int sdg_last_error(char* buf, int n);
+
+/* --- forward ------------------------------------------------------------------- */
+
+/* UNet forward with HOST buffers (north-star unet_forward(latent, timestep,
+ * context); replaces Java_..._unetForward, vk_engine.cpp:875-887, whose
+ * caller precomputes the 320-d sinusoid — pass timesteps instead).
+ *   latent    [B,4,H,W] fp32 (H, W multiples of 8, <= 128)
+ *   timesteps [n_t] fp32, n_t == 1 (shared) or B
+ *   context   [B,77,768] fp32
+ *   out       [B,4,H,W] fp32 (eps prediction)
+ * stream may be NULL (engine stream). Synchronous. */
+SDG_API int sdg_unet_forward(sdg_engine* e, const float* latent, const float* timesteps, int n_t,
+                             const float* context, int B, int H, int W, float* out, void* stream);
+
+/* Same, but with the reference's precomputed 320-d time projection
+ * ([n_t,320] fp32, cos first) in place of timesteps — the exact argument list
+ * of Java_..._unetForward (vk_engine.cpp:875-887). */
+SDG_API int sdg_unet_forward_tproj(sdg_engine* e, const float* latent, const float* temb_proj, int n_t,
+                                   const float* context, int B, int H, int W, float* out, void* stream);
+
+/* Device-pointer variant: same layouts, all pointers on the engine's device;
+ * asynchronous on `stream` (NULL = engine stream). */
+SDG_API int sdg_unet_forward_device(sdg_engine* e, const float* latent, const float* timesteps, int n_t,
+                                    const float* context, int B, int H, int W, float* out, void* stream);
+
+/* Batch-CFG forward, replaces Java_..._unetForward2 (vk_engine.cpp:891-913):
+ * one latent [4,H,W], one timestep, cond and uncond contexts [77,768];
+ * out2 = [cond eps (4HW) ; uncond eps (4HW)]. Runs one B=2 forward. */
+SDG_API int sdg_unet_forward_cfg(sdg_engine* e, const float* latent, float timestep, const float* cond,
+                                 const float* uncond, int H, int W, float* out2);
+
+/* 4-step LCM denoise with batch-CFG per image (VulkanUnetPipeline.kt:63-97 +
+ * LcmScheduler.kt): n_img latents [n_img,4,H,W] (initial noise), cond/uncond
+ * contexts [n_img,77,768] each, step noise [steps-1, n_img,4,H,W] (host
+ * generated, used between steps), cfg scale. Writes final latents to out.
+ * The CFG combine and the LCM update run on the device. */
+SDG_API int sdg_lcm_denoise(sdg_engine* e, const float* latents, const float* cond, const float* uncond,
+                            const float* step_noise, int n_img, int H, int W, int steps, float cfg, float* out);
+
+/* Per-category device times of one eager forward (replaces
+ * Java_..._unetProfile, vk_engine.cpp:854-872, which only logs). Returns the
+ * number of rows written (<= cap) or a negative status. */
+SDG_API int sdg_profile(sdg_engine* e, int B, int H, int W, sdg_profile_row* rows, int cap);
+
+/* Number of kernel launches of one forward at (B,H,W) (after a forward ran). */
+SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
+
+/* --- operator surface (device pointers, fp16 NHWC, stream may be NULL) -------------
+ * Replaces the engine's internal op wrappers conv / matmul / groupnorm(_silu) /
+ * layernorm / attention op / addbias / addv / concat / upsample
+ * (vk_engine.cpp:546-697). Weights here are in ENGINE layout:
+ *   conv weight   [Co][k*k][Ci1+Ci2]   (k = 3 or 1; tap-major, channel-minor)
+ *   linear weight [N][K]               (K-major, i.e. PyTorch [out,in])
+ * err_word: device int zeroed by the caller; a kernel whose bounded wait
+ * expires writes a non-zero code there (NULL: the op uses an internal word). */
+
+/* y = conv(x) (+bias[Co]) (+rowbias[b,Co]) (+residual) (act: 0 none, 1 SiLU).
+ * x is [B,H,W,Ci1], x2 (optional, channel concat after x) [B,H,W,Ci2].
+ * k = 3 (pad 1, stride 1 or 2) or 1. y is [B,Ho,Wo,Co]. For stride 2 the
+ * caller supplies col_scratch of B*Ho*Wo*9*Ci fp16 (else NULL). */
+SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int W, int Ci1, int Ci2,
+                       const uint16_t* w, const float* bias, int Co, int k, int stride, const float* rowbias,
+                       const uint16_t* residual, int act, uint16_t* y, uint16_t* col_scratch, int* err_word,
+                       void* stream);
+
+/* y[M,N] = x[M,K] * w[N,K]^T (+bias) (+residual) (act: 0 none, 1 SiLU,
+ * 2 GEGLU: w rows arranged in 256-row tiles [128 value rows ; 128 gate rows],
+ * y is [M, N/2]). */
+SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
+                       const uint16_t* residual, int act, uint16_t* y, int* err_word, void* stream);
+
+/* GroupNorm(groups) (+SiLU) over x (optionally channel-concat [x ; x2]),
+ * [B,HW,C1+C2] -> y. stats_scratch: device fp32[B*(C1+C2)*2], any contents
+ * (zeroed here). */
+SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,
+                          const float* gamma, const float* beta, float eps, int silu, uint16_t* y,
+                          float* stats_scratch, void* stream);
+
+SDG_API int sdg_layernorm(const uint16_t* x, int M, int C, const float* gamma, const float* beta, float eps,
+                          uint16_t* y, void* stream);
+
+/* Multi-head attention with per-image keys. q [BH,Sq,dp], k [BH,Sk,dp]
+ * (dp = d rounded up to 64), v TRANSPOSED [BH,d16,vt_ld] (d16 = d rounded up
+ * to 16, vt_ld >= Sk, multiple of 8); all padding zero. o [B,Sq,heads*d]. */
+SDG_API int sdg_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int heads, int Sq,
+                          int Sk, int d, int vt_ld, uint16_t* o, int* err_word, void* stream);
+
+SDG_API int sdg_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* y, void* stream);
+SDG_API int sdg_concat(const uint16_t* a, int Ca, const uint16_t* b, int Cb, int rows, uint16_t* y, void* stream);
+SDG_API int sdg_upsample2x(const uint16_t* x, int B, int H, int W, int C, uint16_t* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SDG_H_ */

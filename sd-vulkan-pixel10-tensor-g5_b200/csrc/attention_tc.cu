@@ -1,0 +1,336 @@
+// attention_tc.cu — fused flash attention for sm_100a (tcgen05 + TMA).
+//
+// Replaces attention_f32.comp / attention_big_f32.comp and the split/merge
+// head shaders (vk_engine.cpp:649-663): softmax(Q K^T / sqrt(d)) V per head,
+// keys restricted to the query's own image, online softmax in fp32.
+//
+// Layout: Q and K arrive in a padded per-head layout [B*heads, S, DP]
+// (DP = d rounded up to 64) and V transposed, [B*heads, D16, S_pad]
+// (D16 = d rounded up to 16), all written by the projection GEMM's epilogue
+// with zero padding. Every operand tile is then a plain 3D TMA box with
+// 128-byte swizzle and both MMAs take K-major operands.
+// CTA = NQT query tiles of 128 rows of one (image, head):
+//   warp 0        TMA producer (Q once, K/V ring of NKV stages)
+//   warp 1        MMA issuer: S_t = Q_t K^T (TMEM), then O_t += P_t V
+//   warps 2..     NQT softmax warpgroups, one TMEM row per thread: max,
+//                 exp2, row sum, fp16 P into swizzled smem (A operand of PV),
+//                 PV folded into register accumulators with the running
+//                 rescale, final 1/l and store.
+// Keys beyond Sk (cross-attention: 77 keys in a 128-key tile) are masked.
+#include <algorithm>
+
+#include "sdg_kernels.h"
+#include "sdg_ptx.cuh"
+#include "sdg_tma.h"
+
+namespace sdg {
+namespace {
+
+template <int DP_, int BKV_, int NQT_, int D16_>
+struct AttnCfg {
+  static constexpr int DP = DP_, BKV = BKV_, NQT = NQT_, D16 = D16_;
+  static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
+  static constexpr int NKV = (DP == 64) ? 3 : 2;              // K/V pipeline depth
+  static constexpr uint32_t kQTile = 128 * 128 * NATOM;       // bytes per 128-row Q tile
+  static constexpr uint32_t kKTile = BKV * 128 * NATOM;       // bytes of K per stage
+  static constexpr uint32_t kVTile = (BKV / 64) * D16 * 128;   // bytes of V^T per stage
+  static constexpr uint32_t kPTile = 128 * BKV * 2;           // fp16 P per query tile
+  static constexpr int PVS = (D16 + 31) / 32 * 32;            // TMEM column stride of PV buffers
+  static constexpr int kTmemNeed = NQT * BKV + NQT * PVS;
+  static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
+  static constexpr int kThreads = 64 + 128 * NQT;
+  static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)NQT * kPTile + 1024;
+};
+
+struct AttnDev {
+  int heads, Sq, Sk, d;
+  __half* o;
+  int ld_o;
+  float sl2;  // scale * log2(e)
+  int* err;
+};
+
+template <class CF>
+__global__ void __launch_bounds__(CF::kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                   const __grid_constant__ CUtensorMap map_v, const AttnDev p) {
+  constexpr int BKV = CF::BKV, NQT = CF::NQT, NKV = CF::NKV, NATOM = CF::NATOM, D16 = CF::D16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + NQT * CF::kQTile;
+  uint8_t* sV = sK + NKV * CF::kKTile;
+  uint8_t* sP = sV + NKV * CF::kVTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + NQT * CF::kPTile);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 64);
+  const uint32_t b0 = smem_u32(bars);
+  // barrier indices
+  const uint32_t q_full = b0;
+  auto kv_full = [&](int s) { return b0 + 8u * (1 + s); };
+  auto kv_empty = [&](int s) { return b0 + 8u * (1 + NKV + s); };
+  auto s_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + t); };
+  auto s_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 2 + t); };
+  auto p_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 + t); };
+  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 6 + t); };
+  auto pv_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 8 + t); };
+  const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 10);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int q0 = blockIdx.x * 128 * NQT;
+  const int nkv = (p.Sk + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < NKV; ++s) { mbar_init(kv_full(s), 1); mbar_init(kv_empty(s), 1); }
+    for (int t = 0; t < NQT; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(s_free(t), 4);
+      mbar_init(p_full(t), 128);
+      mbar_init(pv_full(t), 1);
+      mbar_init(pv_free(t), 4);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), CF::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(q_full, NQT * CF::kQTile);
+      for (int t = 0; t < NQT; ++t)
+        for (int a = 0; a < NATOM; ++a)
+          tma_load_3d(smem_u32(sQ + t * CF::kQTile + a * 16384), &map_q, q_full, 64 * a, q0 + 128 * t, bh);
+      bool issued[NKV];
+      int last_ph[NKV];
+      for (int s = 0; s < NKV; ++s) { issued[s] = false; last_ph[s] = 0; }
+      bool ok = true;
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % NKV;
+        const uint32_t ph = (j / NKV) & 1;
+        if (!mbar_wait(kv_empty(s), ph ^ 1u, p.err, kDevTimeoutAttn)) { ok = false; break; }
+        mbar_arrive_expect_tx(kv_full(s), CF::kKTile + CF::kVTile);
+        issued[s] = true;
+        last_ph[s] = ph;
+        for (int a = 0; a < NATOM; ++a)
+          tma_load_3d(smem_u32(sK + s * CF::kKTile + a * BKV * 128), &map_k, kv_full(s), 64 * a, j * BKV, bh);
+        for (int a = 0; a < BKV / 64; ++a)
+          tma_load_3d(smem_u32(sV + s * CF::kVTile + a * D16 * 128), &map_v, kv_full(s), j * BKV + 64 * a, 0, bh);
+      }
+      if (!ok) {
+        mbar_wait(q_full, 0, p.err, kDevTimeoutDrain);
+        for (int s = 0; s < NKV; ++s)
+          if (issued[s]) mbar_wait(kv_full(s), (uint32_t)last_ph[s], p.err, kDevTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = idesc_f16(128, BKV, false);
+      const uint32_t idesc_o = idesc_f16(128, D16, false);
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn) && mbar_wait(kv_full(0), 0, p.err, kDevTimeoutAttn);
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t d_s = tmem + t * BKV;
+        for (int kk = 0; kk < D16 / 16; ++kk) {
+          const int a = kk >> 2;
+          const uint64_t da = sdesc_sw128(smem_u32(sQ + t * CF::kQTile + a * 16384) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = sdesc_sw128(smem_u32(sK + s * CF::kKTile + a * BKV * 128) + (kk & 3) * 32, 16, 1024);
+          mma_f16_ss(d_s, da, db, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(s_full(t));
+      };
+      auto issue_pv = [&](int t, int s) {
+        const uint32_t d_o = tmem + NQT * BKV + t * CF::PVS;
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const int a = kk >> 2;
+          const uint64_t da = sdesc_sw128(smem_u32(sP + t * CF::kPTile + a * 16384) + (kk & 3) * 32, 16, 1024);
+          // V^T tile: D16 rows (output dims) x 64 keys per atom, K-major over keys
+          const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * D16 * 128) + (kk & 3) * 32, 16, 1024);
+          mma_f16_ss(d_o, da, db, idesc_o, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(pv_full(t));
+      };
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < NQT; ++t) issue_qk(t, 0);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv) {
+          const int s1 = (j + 1) % NKV;
+          if (!mbar_wait(kv_full(s1), ((j + 1) / NKV) & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+          for (int t = 0; t < NQT; ++t) {
+            if (!mbar_wait(s_free(t), j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(t, s1);
+          }
+          if (!ok) break;
+        }
+        for (int t = 0; t < NQT; ++t) {
+          if (!mbar_wait(p_full(t), j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+          if (j > 0 && !mbar_wait(pv_free(t), (j - 1) & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j % NKV);
+        }
+        if (!ok) break;
+        mma_commit(kv_empty(j % NKV));
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.err, kDevTimeoutDrain);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int sw = warp - 2;        // 0 .. 4*NQT-1
+    const int t = sw >> 2;          // query tile of this warpgroup
+    const int lg = warp & 3;        // TMEM lane group
+    const int row = lg * 32 + lane; // row within the query tile
+    const uint32_t lane_off = static_cast<uint32_t>(lg * 32) << 16;
+    const uint32_t t_s = tmem + t * BKV + lane_off;
+    const uint32_t t_o = tmem + NQT * BKV + t * CF::PVS + lane_off;
+    uint8_t* prow = sP + t * CF::kPTile + row * 128;
+    const int r7 = row & 7;
+    float O[D16];
+#pragma unroll
+    for (int i = 0; i < D16; ++i) O[i] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      ok = mbar_wait(s_full(t), j & 1, p.err, kDevTimeoutAttn);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int kbase = j * BKV;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_s + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (kbase + c + e < p.Sk) mx = fmaxf(mx, __uint_as_float(r[e]));
+      }
+      const float m_new = fmaxf(m, mx * p.sl2);
+      const float corr = ex2_approx(m - m_new);
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_s + c, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float p0 = (kbase + c + e < p.Sk) ? ex2_approx(__uint_as_float(r[e]) * p.sl2 - m_new) : 0.f;
+          const float p1 = (kbase + c + e + 1 < p.Sk) ? ex2_approx(__uint_as_float(r[e + 1]) * p.sl2 - m_new) : 0.f;
+          rs += p0 + p1;
+          pk[e >> 1] = pack_half2(p0, p1);
+        }
+        // 32 keys = four 16-byte chunks of the 128B-swizzled K-major row
+        const int atom = c >> 6;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((c & 63) >> 3) + q;
+          uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(prow + atom * 16384 + ((chunk ^ r7) << 4)) = u;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free(t));
+      fence_proxy_async_smem();
+      mbar_arrive(p_full(t));
+      l = l * corr + rs;
+      m = m_new;
+      ok = mbar_wait(pv_full(t), j & 1, p.err, kDevTimeoutAttn);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D16; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_o + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) O[c + e] = O[c + e] * corr + __uint_as_float(r[e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pv_free(t));
+    }
+    const int qi = q0 + t * 128 + row;
+    if (ok && qi < p.Sq) {
+      const float inv = 1.f / l;
+      const int b = bh / p.heads, h = bh % p.heads;
+      __half* dst = p.o + ((size_t)b * p.Sq + qi) * p.ld_o + (size_t)h * p.d;
+#pragma unroll
+      for (int c = 0; c < D16; c += 8) {
+        if (c >= p.d) break;
+        uint4 u;
+        u.x = pack_half2(O[c + 0] * inv, O[c + 1] * inv);
+        u.y = pack_half2(O[c + 2] * inv, O[c + 3] * inv);
+        u.z = pack_half2(O[c + 4] * inv, O[c + 5] * inv);
+        u.w = pack_half2(O[c + 6] * inv, O[c + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + c) = u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, CF::kTmemCols);
+  }
+}
+
+template <class CF>
+cudaError_t launch_cfg(const AttnArgs& a, int* err, cudaStream_t s) {
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<CF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CF::kSmem);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  CUtensorMap mq{}, mk{}, mv{};
+  auto mk3 = [&](CUtensorMap* m, const __half* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+    uint64_t dims[3] = {inner, rows, (uint64_t)a.BH};
+    uint64_t str[2] = {inner * 2, rows * inner * 2};
+    uint32_t box[3] = {64, box_rows, 1};
+    return make_tmap(m, base, 3, dims, str, box);
+  };
+  if (!mk3(&mq, a.q, CF::DP, a.Sq, 128) || !mk3(&mk, a.k, CF::DP, a.Sk, CF::BKV) ||
+      !mk3(&mv, a.v, a.vt_ld, CF::D16, CF::D16))
+    return cudaErrorInvalidValue;
+  AttnDev d{a.heads, a.Sq, a.Sk, a.d, a.o, a.ld_o, a.scale * 1.4426950408889634f, err};
+  dim3 grid((a.Sq + 128 * CF::NQT - 1) / (128 * CF::NQT), a.BH);
+  attn_tc_kernel<CF><<<grid, CF::kThreads, CF::kSmem, s>>>(mq, mk, mv, d);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
+  if (a.BH <= 0 || a.heads <= 0 || a.Sq <= 0 || a.Sk <= 0 || a.d % 8 || !a.q || !a.k || !a.v || !a.o)
+    return cudaErrorInvalidValue;
+  const int dp = (a.d + 63) / 64 * 64;
+  if (a.dp != dp || a.vt_ld < a.Sk || a.vt_ld % 8 || a.d16 != (a.d + 15) / 16 * 16) return cudaErrorInvalidValue;
+  switch (a.d16) {
+    case 48: return launch_cfg<AttnCfg<64, 128, 2, 48>>(a, err, s);
+    case 64: return launch_cfg<AttnCfg<64, 128, 2, 64>>(a, err, s);
+    case 80: return launch_cfg<AttnCfg<128, 128, 2, 80>>(a, err, s);
+    case 160: return launch_cfg<AttnCfg<192, 64, 1, 160>>(a, err, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace sdg

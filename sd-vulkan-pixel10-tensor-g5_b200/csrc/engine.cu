@@ -1,0 +1,1086 @@
+// engine.cu — the SD1.5 UNet engine behind the C ABI (include/sdg.h).
+//
+// Replaces namespace unet of the reference (vk_engine.cpp:482-926):
+//   W()/WC_ weight cache        -> Weights: reference-format fp16 blobs are
+//                                  uploaded once, re-laid-out for the kernels
+//                                  (conv [Co][tap][Ci], linear [N][K], fused
+//                                  QKV / cross-KV / GEGLU-tiled FF) into one
+//                                  device weight arena
+//   runGraph + one VkCommandBuffer -> Plan: the forward is issued by build()
+//                                  into a bump-allocated activation arena and
+//                                  captured once per (B,H,W) as a CUDA graph;
+//                                  each call replays the graph
+//   SCRATCH_ per-forward mallocs   -> none: the arena is sized by a dry run of
+//                                  build() and reused for every forward
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/sdg.h"
+#include "sdg_kernels.h"
+
+namespace sdg {
+
+static thread_local std::string g_last_error;
+static int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+int op_fail(int code, const std::string& msg) { return fail(code, msg); }
+#define SDG_CUDA_TRY(x)                                                                  \
+  do {                                                                                   \
+    cudaError_t _e = (x);                                                                \
+    if (_e != cudaSuccess) return fail(SDG_ERR_CUDA, std::string(#x) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+static const int kBlockOut[4] = {320, 640, 1280, 1280};
+static const int kHeads = 8;
+static const int kCtxLen = 77, kCtxDim = 768, kTemb = 1280;
+static const float kResEps = 1e-5f, kTfGnEps = 1e-6f, kLnEps = 1e-5f;
+static const int kCtxPad = 80;  // cross-attention V^T row length (77 keys, padded to a 16-byte multiple)
+
+// ------------------------------------------------------------------ weights
+struct HostWeight {
+  std::vector<uint16_t> data;
+  std::vector<int64_t> shape;
+};
+struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; };
+struct Norm { float* g = nullptr; float* b = nullptr; int C = 0; };
+struct ConvW { __half* w = nullptr; float* b = nullptr; int Co = 0, Ci = 0, k = 3; };
+struct ResW { Norm n1, n2; ConvW c1, c2; bool has_sc = false; Lin sc; int tp_off = 0, cin = 0, cout = 0; };
+struct TfW { Norm gn, ln1, ln2, ln3; Lin pin, qkv, out1, q2, kv2, out2, ff1, ff2, pout; int C = 0; };
+struct UNetW {
+  Lin t1, t2;
+  ConvW conv_in, conv_out;
+  Norm norm_out;
+  ResW down_res[4][2];
+  TfW down_tf[3][2];
+  ConvW down_ds[3];
+  ResW mid_res[2];
+  TfW mid_tf;
+  ResW up_res[4][3];
+  TfW up_tf[4][3];  // [0][*] unused
+  ConvW up_us[3];
+  __half* tp_w = nullptr;
+  float* tp_b = nullptr;
+  int tp_N = 0;
+};
+
+// ------------------------------------------------------------------ arena builder
+struct Buf {
+  __half* p = nullptr;
+  int C = 0;
+};
+struct AttnBufs {  // per (level) self-attention operands, zero padded, persistent
+  __half* q = nullptr; __half* k = nullptr; __half* vt = nullptr;
+};
+struct CrossBufs { __half* k = nullptr; __half* vt = nullptr; };
+
+enum Cat { kCatGN = 0, kCatLN, kCatConv3, kCatGemm, kCatAttn, kCatGemv, kCatMisc, kCatCount };
+static const char* kCatName[kCatCount] = {"GN", "LN", "CONV3", "GEMM", "ATTN", "GEMV", "MISC"};
+
+struct Plan {
+  int B = 0, H = 0, W = 0, mode = 0;  // mode 0: timesteps, 1: precomputed tproj
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  // io
+  float* lat_in = nullptr; float* t_in = nullptr; float* tproj_in = nullptr; float* ctx_in = nullptr;
+  float* out = nullptr;
+  int* dev_err = nullptr;
+  int launches = 0;
+};
+
+struct Engine;
+
+class Builder {
+ public:
+  Builder(Engine& e, Plan& pl, bool dry, cudaStream_t s) : e_(e), pl_(pl), dry_(dry), s_(s) {}
+  int run();  // issues the whole forward; returns SDG status
+  size_t peak() const { return peak_; }
+  int launches() const { return launches_; }
+  // profiling: per-launch category events
+  bool profile = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof;
+
+ private:
+  Engine& e_;
+  Plan& pl_;
+  bool dry_;
+  cudaStream_t s_;
+  size_t off_ = 0, peak_ = 0;
+  int launches_ = 0;
+  int status_ = SDG_OK;
+  int gn_slot_ = 0;
+  float* gn_stats_ = nullptr;
+  size_t gn_slot_floats_ = 0;
+  std::map<long, AttnBufs> attn_;
+  std::vector<CrossBufs> cross_;
+  int cross_idx_ = 0;
+  float* tp_all_ = nullptr;
+  __half* ctx16_ = nullptr;
+
+  void* alloc(size_t bytes) {
+    size_t o = (off_ + 255) & ~size_t(255);
+    off_ = o + bytes;
+    if (off_ > peak_) peak_ = off_;
+    return dry_ ? nullptr : pl_.arena + o;
+  }
+  __half* alloc_h(size_t n) { return static_cast<__half*>(alloc(n * 2)); }
+  float* alloc_f(size_t n) { return static_cast<float*>(alloc(n * 4)); }
+
+  bool ok() const { return status_ == SDG_OK; }
+  void check(cudaError_t err, const char* what, int cat, int nk = 1);
+  void begin_op(int cat);
+  cudaEvent_t ev_start_ = nullptr;
+
+  // ops
+  void gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, float eps, bool silu, __half* y);
+  void gemm(GemmArgs a, int cat);
+  Buf resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W);
+  Buf transformer(const TfW& t, const Buf& x, int H, int W);
+  Buf downsample(const ConvW& c, const Buf& x, int H, int W);
+  Buf upsample(const ConvW& c, const Buf& x, int H, int W);
+  AttnBufs& level_bufs(int C, int S);
+};
+
+struct Engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::unordered_map<std::string, HostWeight> host;
+  bool prepared = false;
+  char* warena = nullptr;
+  size_t warena_bytes = 0;
+  UNetW w;
+  std::map<long, std::unique_ptr<Plan>> plans;
+  int* op_err = nullptr;  // error word for op-surface calls without one
+  ~Engine();
+  int prepare();
+  int get_plan(int B, int H, int W, int mode, Plan** out);
+  int run_plan(Plan* p, cudaStream_t s);
+  int check_dev_err(Plan* p, cudaStream_t s);
+};
+
+// ------------------------------------------------------------------ weight preparation
+namespace {
+
+float h2f(uint16_t h) {
+  __half_raw r;
+  r.x = h;
+  return __half2float(__half(r));
+}
+
+struct WeightPacker {
+  Engine& e;
+  std::vector<char> staging;  // host image of the device weight arena
+  size_t off = 0;
+  std::vector<std::pair<size_t, void**>> fixups;
+  std::string missing;
+  explicit WeightPacker(Engine& en) : e(en) {}
+
+  const HostWeight* get(const std::string& k, size_t numel) {
+    auto it = e.host.find(k);
+    if (it == e.host.end() || it->second.data.size() != numel) {
+      if (missing.empty()) missing = k + (it == e.host.end() ? " (missing)" : " (wrong size)");
+      return nullptr;
+    }
+    return &it->second;
+  }
+  size_t reserve(size_t bytes) {
+    size_t o = (off + 255) & ~size_t(255);
+    off = o + bytes;
+    if (staging.size() < off) staging.resize(std::max(off, staging.size() * 2));
+    return o;
+  }
+  template <class T>
+  void place(T** dst, size_t o) { fixups.push_back({o, reinterpret_cast<void**>(dst)}); }
+
+  void vecf(float** dst, const std::string& k, int n) {
+    size_t o = reserve((size_t)n * 4);
+    place(dst, o);
+    const HostWeight* hw = get(k, n);
+    float* f = reinterpret_cast<float*>(staging.data() + o);
+    for (int i = 0; i < n; ++i) f[i] = hw ? h2f(hw->data[i]) : 0.f;
+  }
+  void norm(Norm& nm, const std::string& pf, int C) {
+    nm.C = C;
+    vecf(&nm.g, pf + ".weight", C);
+    vecf(&nm.b, pf + ".bias", C);
+  }
+  // Linear stored [in,out] in the reference format -> [out][in] rows placed at row offset `row0` of `dst_o`.
+  void linear_rows(size_t dst_o, int row0, int ld, const std::string& k, int in, int out) {
+    const HostWeight* hw = get(k, (size_t)in * out);
+    uint16_t* d = reinterpret_cast<uint16_t*>(staging.data() + dst_o);
+    for (int o = 0; o < out; ++o)
+      for (int i = 0; i < in; ++i) d[(size_t)(row0 + o) * ld + i] = hw ? hw->data[(size_t)i * out + o] : 0;
+  }
+  void linear(Lin& L, const std::string& pf, int in, int out, bool bias) {
+    L.N = out; L.K = in;
+    size_t o = reserve((size_t)in * out * 2);
+    place(&L.w, o);
+    linear_rows(o, 0, in, pf + ".weight", in, out);
+    if (bias) vecf(&L.b, pf + ".bias", out);
+  }
+  // conv [Co,Ci,k,k] -> [Co][k*k][Ci] (1x1: [Co][Ci])
+  void conv(ConvW& c, const std::string& pf, int ci, int co, int k) {
+    c.Co = co; c.Ci = ci; c.k = k;
+    size_t o = reserve((size_t)co * ci * k * k * 2);
+    place(&c.w, o);
+    const HostWeight* hw = get(pf + ".weight", (size_t)co * ci * k * k);
+    uint16_t* d = reinterpret_cast<uint16_t*>(staging.data() + o);
+    for (int oc = 0; oc < co; ++oc)
+      for (int ic = 0; ic < ci; ++ic)
+        for (int t = 0; t < k * k; ++t)
+          d[((size_t)oc * k * k + t) * ci + ic] = hw ? hw->data[((size_t)oc * ci + ic) * k * k + t] : 0;
+    vecf(&c.b, pf + ".bias", co);
+  }
+  void conv1x1_as_linear(Lin& L, const std::string& pf, int ci, int co) {
+    ConvW c;
+    conv(c, pf, ci, co, 1);
+    // the fixups recorded pointers into c; re-target them at L
+    fixups[fixups.size() - 2].second = reinterpret_cast<void**>(&L.w);
+    fixups[fixups.size() - 1].second = reinterpret_cast<void**>(&L.b);
+    L.N = co; L.K = ci;
+  }
+};
+
+}  // namespace
+
+int Engine::prepare() {
+  if (prepared) return SDG_OK;
+  WeightPacker P(*this);
+  w.t1 = Lin{}; w.t2 = Lin{};
+  P.linear(w.t1, "time_embedding.linear_1", 320, kTemb, true);
+  P.linear(w.t2, "time_embedding.linear_2", kTemb, kTemb, true);
+  // conv_in: [320][tap*4 + c] padded to K = 64
+  {
+    w.conv_in.Co = 320; w.conv_in.Ci = 4; w.conv_in.k = 3;
+    size_t o = P.reserve(320 * 64 * 2);
+    P.place(&w.conv_in.w, o);
+    const HostWeight* hw = P.get("conv_in.weight", 320 * 4 * 9);
+    uint16_t* d = reinterpret_cast<uint16_t*>(P.staging.data() + o);
+    for (int oc = 0; oc < 320; ++oc)
+      for (int k = 0; k < 64; ++k) {
+        uint16_t v = 0;
+        if (k < 36 && hw) { const int tap = k / 4, c = k % 4; v = hw->data[((size_t)oc * 4 + c) * 9 + tap]; }
+        d[(size_t)oc * 64 + k] = v;
+      }
+    P.vecf(&w.conv_in.b, "conv_in.bias", 320);
+  }
+  // time_emb_proj of every ResNet, batched: rows in graph order
+  std::vector<std::pair<std::string, ResW*>> resnets;
+  auto res = [&](ResW& r, const std::string& pf, int cin, int cout) {
+    r.cin = cin; r.cout = cout;
+    P.norm(r.n1, pf + ".norm1", cin);
+    P.conv(r.c1, pf + ".conv1", cin, cout, 3);
+    P.norm(r.n2, pf + ".norm2", cout);
+    P.conv(r.c2, pf + ".conv2", cout, cout, 3);
+    r.has_sc = cin != cout;
+    if (r.has_sc) P.conv1x1_as_linear(r.sc, pf + ".conv_shortcut", cin, cout);
+    resnets.push_back({pf, &r});
+  };
+  auto tf = [&](TfW& t, const std::string& pf, int C) {
+    t.C = C;
+    const std::string b = pf + ".transformer_blocks.0";
+    P.norm(t.gn, pf + ".norm", C);
+    P.conv1x1_as_linear(t.pin, pf + ".proj_in", C, C);
+    P.norm(t.ln1, b + ".norm1", C);
+    P.norm(t.ln2, b + ".norm2", C);
+    P.norm(t.ln3, b + ".norm3", C);
+    {  // fused QKV [3C][C]
+      t.qkv.N = 3 * C; t.qkv.K = C;
+      size_t o = P.reserve((size_t)3 * C * C * 2);
+      P.place(&t.qkv.w, o);
+      P.linear_rows(o, 0, C, b + ".attn1.to_q.weight", C, C);
+      P.linear_rows(o, C, C, b + ".attn1.to_k.weight", C, C);
+      P.linear_rows(o, 2 * C, C, b + ".attn1.to_v.weight", C, C);
+    }
+    P.linear(t.out1, b + ".attn1.to_out.0", C, C, true);
+    P.linear(t.q2, b + ".attn2.to_q", C, C, false);
+    {  // fused cross K/V [2C][768]
+      t.kv2.N = 2 * C; t.kv2.K = kCtxDim;
+      size_t o = P.reserve((size_t)2 * C * kCtxDim * 2);
+      P.place(&t.kv2.w, o);
+      P.linear_rows(o, 0, kCtxDim, b + ".attn2.to_k.weight", kCtxDim, C);
+      P.linear_rows(o, C, kCtxDim, b + ".attn2.to_v.weight", kCtxDim, C);
+    }
+    P.linear(t.out2, b + ".attn2.to_out.0", C, C, true);
+    {  // GEGLU proj [8C][C] re-tiled: each 256-row tile = [128 value rows ; 128 gate rows]
+      const int N = 8 * C, half = 4 * C;
+      t.ff1.N = N; t.ff1.K = C;
+      size_t tmp = P.reserve((size_t)N * C * 2);
+      P.linear_rows(tmp, 0, C, b + ".ff.net.0.proj.weight", C, N);
+      size_t o = P.reserve((size_t)N * C * 2);
+      P.place(&t.ff1.w, o);
+      size_t bo = P.reserve((size_t)N * 4);
+      P.place(&t.ff1.b, bo);
+      const HostWeight* hb = P.get(b + ".ff.net.0.proj.bias", N);
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(P.staging.data() + tmp);
+      uint16_t* dst = reinterpret_cast<uint16_t*>(P.staging.data() + o);
+      float* bd = reinterpret_cast<float*>(P.staging.data() + bo);
+      for (int r = 0; r < N; ++r) {
+        const int tile = r / 256, within = r % 256;
+        const int srow = within < 128 ? tile * 128 + within : half + tile * 128 + (within - 128);
+        memcpy(dst + (size_t)r * C, src + (size_t)srow * C, (size_t)C * 2);
+        bd[r] = hb ? h2f(hb->data[srow]) : 0.f;
+      }
+    }
+    P.linear(t.ff2, b + ".ff.net.2", 4 * C, C, true);
+    P.conv1x1_as_linear(t.pout, pf + ".proj_out", C, C);
+  };
+  char pf[96];
+  int cprev = 320;
+  for (int i = 0; i < 4; ++i) {
+    const int cout = kBlockOut[i];
+    for (int r = 0; r < 2; ++r) {
+      snprintf(pf, sizeof pf, "down_blocks.%d.resnets.%d", i, r);
+      res(w.down_res[i][r], pf, r == 0 ? cprev : cout, cout);
+      if (i < 3) {
+        snprintf(pf, sizeof pf, "down_blocks.%d.attentions.%d", i, r);
+        tf(w.down_tf[i][r], pf, cout);
+      }
+    }
+    if (i < 3) {
+      snprintf(pf, sizeof pf, "down_blocks.%d.downsamplers.0.conv", i);
+      P.conv(w.down_ds[i], pf, cout, cout, 3);
+    }
+    cprev = cout;
+  }
+  res(w.mid_res[0], "mid_block.resnets.0", 1280, 1280);
+  tf(w.mid_tf, "mid_block.attentions.0", 1280);
+  res(w.mid_res[1], "mid_block.resnets.1", 1280, 1280);
+  {
+    int skip_ch[12] = {320, 320, 320, 320, 640, 640, 640, 1280, 1280, 1280, 1280, 1280};
+    int ns = 12;
+    const int up_out[4] = {1280, 1280, 640, 320};
+    cprev = 1280;
+    for (int i = 0; i < 4; ++i) {
+      for (int r = 0; r < 3; ++r) {
+        const int cs = skip_ch[--ns];
+        snprintf(pf, sizeof pf, "up_blocks.%d.resnets.%d", i, r);
+        res(w.up_res[i][r], pf, cprev + cs, up_out[i]);
+        cprev = up_out[i];
+        if (i > 0) {
+          snprintf(pf, sizeof pf, "up_blocks.%d.attentions.%d", i, r);
+          tf(w.up_tf[i][r], pf, up_out[i]);
+        }
+      }
+      if (i < 3) {
+        snprintf(pf, sizeof pf, "up_blocks.%d.upsamplers.0.conv", i);
+        P.conv(w.up_us[i], pf, up_out[i], up_out[i], 3);
+      }
+    }
+  }
+  P.norm(w.norm_out, "conv_norm_out", 320);
+  P.conv(w.conv_out, "conv_out", 320, 4, 3);
+  // batched time_emb_proj [sum Cout][1280]
+  {
+    int total = 0;
+    for (auto& pr : resnets) { pr.second->tp_off = total; total += pr.second->cout; }
+    w.tp_N = total;
+    size_t o = P.reserve((size_t)total * kTemb * 2);
+    P.place(&w.tp_w, o);
+    size_t bo = P.reserve((size_t)total * 4);
+    P.place(&w.tp_b, bo);
+    float* bd = reinterpret_cast<float*>(P.staging.data() + bo);
+    for (auto& pr : resnets) {
+      P.linear_rows(o, pr.second->tp_off, kTemb, pr.first + ".time_emb_proj.weight", kTemb, pr.second->cout);
+      const HostWeight* hb = P.get(pr.first + ".time_emb_proj.bias", pr.second->cout);
+      for (int c = 0; c < pr.second->cout; ++c) bd[pr.second->tp_off + c] = hb ? h2f(hb->data[c]) : 0.f;
+    }
+  }
+  if (!P.missing.empty()) return fail(SDG_ERR_MISSING_WEIGHT, "weight " + P.missing);
+  SDG_CUDA_TRY(cudaSetDevice(device));
+  SDG_CUDA_TRY(cudaMalloc(&warena, P.off));
+  warena_bytes = P.off;
+  SDG_CUDA_TRY(cudaMemcpy(warena, P.staging.data(), P.off, cudaMemcpyHostToDevice));
+  for (auto& f : P.fixups) *f.second = warena + f.first;
+  host.clear();
+  prepared = true;
+  return SDG_OK;
+}
+
+// ------------------------------------------------------------------ builder ops
+void Builder::begin_op(int cat) {
+  (void)cat;
+  if (profile && !dry_) {
+    cudaEventCreate(&ev_start_);
+    cudaEventRecord(ev_start_, s_);
+  }
+}
+
+void Builder::check(cudaError_t err, const char* what, int cat, int nk) {
+  launches_ += nk;
+  if (profile && !dry_) {
+    cudaEvent_t e2;
+    cudaEventCreate(&e2);
+    cudaEventRecord(e2, s_);
+    prof.push_back({cat, {ev_start_, e2}});
+  }
+  if (err != cudaSuccess && status_ == SDG_OK) {
+    status_ = SDG_ERR_CUDA;
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(err);
+  }
+}
+
+void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, float eps, bool silu, __half* y) {
+  GroupNormArgs a;
+  a.x0 = x.p; a.C0 = x.C;
+  a.x1 = x2 ? x2->p : nullptr; a.C1 = x2 ? x2->C : 0;
+  a.B = B; a.HW = HW; a.groups = 32;
+  a.gamma = n.g; a.beta = n.b; a.eps = eps; a.silu = silu ? 1 : 0; a.y = y;
+  a.stats = dry_ ? nullptr : gn_stats_ + (size_t)gn_slot_ * gn_slot_floats_;
+  gn_slot_++;
+  if (dry_ || !ok()) { launches_ += 2; return; }
+  begin_op(kCatGN);
+  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 2);
+}
+
+void Builder::gemm(GemmArgs a, int cat) {
+  if (dry_ || !ok()) { launches_ += 1; return; }
+  begin_op(cat);
+  check(launch_gemm(a, pl_.dev_err, s_), cat == kCatConv3 ? "conv3x3" : "gemm", cat);
+}
+
+AttnBufs& Builder::level_bufs(int C, int S) {
+  const long key = (long)C * 1000000 + S;
+  auto it = attn_.find(key);
+  if (it != attn_.end()) return it->second;
+  const int d = C / kHeads, dp = (d + 63) / 64 * 64, d16 = (d + 15) / 16 * 16;
+  const size_t BH = (size_t)pl_.B * kHeads;
+  AttnBufs b;
+  b.q = alloc_h(BH * S * dp);
+  b.k = alloc_h(BH * S * dp);
+  b.vt = alloc_h(BH * d16 * S);
+  return attn_[key] = b;
+}
+
+Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
+  const int B = pl_.B, HW = H * W, M = B * HW;
+  Buf out{alloc_h((size_t)M * r.cout), r.cout};
+  const size_t mark = off_;
+  __half* h = alloc_h((size_t)M * r.cin);
+  gn(x, x2, B, HW, r.n1, kResEps, true, h);
+  __half* h2 = alloc_h((size_t)M * r.cout);
+  {
+    GemmArgs a;
+    a.M = M; a.N = r.cout; a.K = 9 * r.cin; a.taps = 9;
+    a.a0 = h; a.cin0 = r.cin; a.B = B; a.H = H; a.W = W;
+    a.w = r.c1.w; a.bias = r.c1.b;
+    a.rowbias = tp_all_ ? tp_all_ + r.tp_off : nullptr; a.rowbias_ld = e_.w.tp_N; a.rows_per_image = HW;
+    a.out = h2;
+    gemm(a, kCatConv3);
+  }
+  __half* h3 = alloc_h((size_t)M * r.cout);
+  gn(Buf{h2, r.cout}, nullptr, B, HW, r.n2, kResEps, true, h3);
+  const __half* resid = x.p;
+  if (r.has_sc) {
+    __half* sc = alloc_h((size_t)M * r.cout);
+    GemmArgs a;
+    a.M = M; a.N = r.cout; a.K = x.C + (x2 ? x2->C : 0); a.taps = 1;
+    a.a0 = x.p; a.cin0 = x.C;
+    if (x2) { a.a1 = x2->p; a.cin1 = x2->C; }
+    a.w = r.sc.w; a.bias = r.sc.b; a.out = sc;
+    gemm(a, kCatGemm);
+    resid = sc;
+  }
+  {
+    GemmArgs a;
+    a.M = M; a.N = r.cout; a.K = 9 * r.cout; a.taps = 9;
+    a.a0 = h3; a.cin0 = r.cout; a.B = B; a.H = H; a.W = W;
+    a.w = r.c2.w; a.bias = r.c2.b; a.residual = resid; a.out = out.p;
+    gemm(a, kCatConv3);
+  }
+  off_ = mark;
+  return out;
+}
+
+Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
+  const int B = pl_.B, S = H * W, M = B * S, C = t.C;
+  const int d = C / kHeads, dp = (d + 63) / 64 * 64, d16 = (d + 15) / 16 * 16;
+  AttnBufs& ab = level_bufs(C, S);
+  CrossBufs& cb = cross_[cross_idx_++];
+  Buf out{alloc_h((size_t)M * C), C};
+  const size_t mark = off_;
+  __half* g = alloc_h((size_t)M * C);
+  gn(x, nullptr, B, S, t.gn, kTfGnEps, false, g);
+  __half* tt = alloc_h((size_t)M * C);
+  __half* hn = alloc_h((size_t)M * C);
+  __half* o = alloc_h((size_t)M * C);
+  __half* gg = alloc_h((size_t)M * 4 * C);
+  auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
+    GemmArgs a;
+    a.M = M; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; a.w = L.w; a.bias = L.b; a.residual = resid; a.out = y;
+    gemm(a, kCatGemm);
+  };
+  auto ln = [&](const __half* xin, const Norm& n) {
+    if (dry_ || !ok()) { launches_++; return; }
+    begin_op(kCatLN);
+    check(launch_layernorm(xin, M, C, n.g, n.b, kLnEps, hn, s_), "layernorm", kCatLN);
+  };
+  auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
+                   int vt_idx, int spad) {
+    GemmArgs a;
+    a.M = Mr; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; a.w = L.w; a.bias = L.b;
+    a.epi = kEpiHeads; a.rows_per_image = rows_per_image;
+    a.head_out[0] = o0; a.head_out[1] = o1; a.head_out[2] = o2;
+    a.head_C = C; a.heads = kHeads; a.head_d = d; a.head_dp = dp;
+    a.head_vt = vt_idx; a.head_d16 = d16; a.head_spad = spad;
+    gemm(a, kCatGemm);
+  };
+  auto attn = [&](const __half* q, const __half* k, const __half* vt, int Sk, int vt_ld) {
+    if (dry_ || !ok()) { launches_++; return; }
+    AttnArgs a;
+    a.q = q; a.k = k; a.v = vt; a.BH = B * kHeads; a.heads = kHeads; a.Sq = S; a.Sk = Sk; a.d = d; a.dp = dp;
+    a.d16 = d16; a.vt_ld = vt_ld; a.o = o; a.ld_o = C; a.scale = 1.0f / sqrtf((float)d);
+    begin_op(kCatAttn);
+    check(launch_attention(a, pl_.dev_err, s_), "attention", kCatAttn);
+  };
+  lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
+  ln(tt, t.ln1);
+  heads(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, S);            // Q, K, V^T
+  attn(ab.q, ab.k, ab.vt, S, S);                                   // self-attention
+  lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
+  ln(tt, t.ln2);
+  heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
+  heads(ctx16_, B * kCtxLen, kCtxDim, t.kv2, kCtxLen, cb.k, cb.vt, nullptr, 1, kCtxPad);  // K, V^T from context
+  attn(ab.q, cb.k, cb.vt, kCtxLen, kCtxPad);                       // cross-attention
+  lin(o, C, t.out2, tt, tt);
+  ln(tt, t.ln3);
+  {
+    GemmArgs a;
+    a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = hn; a.cin0 = C; a.w = t.ff1.w; a.bias = t.ff1.b;
+    a.epi = kEpiGeglu; a.out = gg; a.ld_out = 4 * C;
+    gemm(a, kCatGemm);
+  }
+  lin(gg, 4 * C, t.ff2, tt, tt);                                   // t += ff(t)
+  lin(tt, C, t.pout, x.p, out.p);                                  // proj_out + x
+  off_ = mark;
+  return out;
+}
+
+Buf Builder::downsample(const ConvW& c, const Buf& x, int H, int W) {
+  const int B = pl_.B, Ho = H / 2, Wo = W / 2, M = B * Ho * Wo;
+  Buf out{alloc_h((size_t)M * c.Co), c.Co};
+  const size_t mark = off_;
+  __half* col = alloc_h((size_t)M * 9 * x.C);
+  if (!dry_ && ok()) {
+    begin_op(kCatMisc);
+    check(launch_im2col3x3(x.p, B, H, W, x.C, 2, 9 * x.C, col, s_), "im2col", kCatMisc);
+  } else {
+    launches_++;
+  }
+  GemmArgs a;
+  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.a0 = col; a.cin0 = 9 * x.C; a.w = c.w; a.bias = c.b; a.out = out.p;
+  gemm(a, kCatGemm);
+  off_ = mark;
+  return out;
+}
+
+Buf Builder::upsample(const ConvW& c, const Buf& x, int H, int W) {
+  const int B = pl_.B, Ho = 2 * H, Wo = 2 * W, M = B * Ho * Wo;
+  Buf out{alloc_h((size_t)M * c.Co), c.Co};
+  const size_t mark = off_;
+  __half* up = alloc_h((size_t)M * x.C);
+  if (!dry_ && ok()) {
+    begin_op(kCatMisc);
+    check(launch_upsample2x(x.p, B, H, W, x.C, up, s_), "upsample", kCatMisc);
+  } else {
+    launches_++;
+  }
+  GemmArgs a;
+  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.taps = 9; a.a0 = up; a.cin0 = x.C; a.B = B; a.H = Ho; a.W = Wo;
+  a.w = c.w; a.bias = c.b; a.out = out.p;
+  gemm(a, kCatConv3);
+  off_ = mark;
+  return out;
+}
+
+int Builder::run() {
+  const int B = pl_.B, H = pl_.H, W = pl_.W, HW = H * W, M = B * HW;
+  const UNetW& w = e_.w;
+  // persistent io + per-level attention operands (zeroed once at plan creation)
+  pl_.lat_in = alloc_f((size_t)B * 4 * HW);
+  pl_.t_in = alloc_f(B);
+  pl_.tproj_in = alloc_f((size_t)B * 320);
+  pl_.ctx_in = alloc_f((size_t)B * kCtxLen * kCtxDim);
+  pl_.out = alloc_f((size_t)B * 4 * HW);
+  pl_.dev_err = static_cast<int*>(alloc(256));
+  gn_slot_floats_ = (size_t)B * 2560 * 2;
+  const int kGnSlots = 64;
+  gn_stats_ = alloc_f(gn_slot_floats_ * kGnSlots);
+  {
+    int h = H, ww = W;
+    for (int i = 0; i < 3; ++i) { level_bufs(kBlockOut[i], h * ww); h /= 2; ww /= 2; }
+    level_bufs(1280, h * ww);  // mid block
+  }
+  cross_.resize(16);
+  for (auto& cb : cross_) {
+    // sized for the widest level (C = 1280: d = 160, dp = 192, d16 = 160)
+    cb.k = alloc_h((size_t)B * kHeads * kCtxLen * 192);
+    cb.vt = alloc_h((size_t)B * kHeads * 160 * kCtxPad);
+  }
+  float* te = alloc_f((size_t)B * 320);
+  float* t1 = alloc_f((size_t)B * kTemb);
+  float* temb = alloc_f((size_t)B * kTemb);
+  tp_all_ = alloc_f((size_t)B * w.tp_N);
+  ctx16_ = alloc_h((size_t)B * kCtxLen * kCtxDim);
+  const size_t persistent_end = off_;
+  (void)persistent_end;
+
+  if (!dry_) {
+    begin_op(kCatMisc);
+    check(cudaMemsetAsync(gn_stats_, 0, gn_slot_floats_ * kGnSlots * 4, s_), "memset", kCatMisc, 0);
+    begin_op(kCatMisc);
+    check(launch_time_embedding(pl_.t_in, B, B, pl_.mode == 1 ? pl_.tproj_in : nullptr, te, s_), "time_embedding", kCatMisc);
+    begin_op(kCatGemv);
+    check(launch_gemv(te, B, 320, w.t1.w, w.t1.b, kTemb, 0, 1, t1, kTemb, s_), "time mlp 1", kCatGemv, (B + 7) / 8);
+    begin_op(kCatGemv);
+    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.b, kTemb, 0, 0, temb, kTemb, s_), "time mlp 2", kCatGemv, (B + 7) / 8);
+    begin_op(kCatGemv);
+    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_b, w.tp_N, 1, 0, tp_all_, w.tp_N, s_), "time_emb_proj", kCatGemv, (B + 7) / 8);
+    begin_op(kCatMisc);
+    check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
+  } else {
+    launches_ += 3 + 3 * ((B + 7) / 8);
+  }
+  // conv_in
+  Buf x{alloc_h((size_t)M * 320), 320};
+  {
+    const size_t mark = off_;
+    __half* col = alloc_h((size_t)M * 64);
+    if (!dry_ && ok()) {
+      begin_op(kCatMisc);
+      check(launch_latent_im2col(pl_.lat_in, B, 4, H, W, 64, col, s_), "latent im2col", kCatMisc);
+    } else {
+      launches_++;
+    }
+    GemmArgs a;
+    a.M = M; a.N = 320; a.K = 64; a.a0 = col; a.cin0 = 64; a.w = w.conv_in.w; a.bias = w.conv_in.b; a.out = x.p;
+    gemm(a, kCatGemm);
+    off_ = mark;
+  }
+  std::vector<Buf> skips{x};
+  int h = H, ww = W;
+  for (int i = 0; i < 4; ++i) {
+    for (int r = 0; r < 2; ++r) {
+      x = resnet(w.down_res[i][r], x, nullptr, h, ww);
+      if (i < 3) x = transformer(w.down_tf[i][r], x, h, ww);
+      skips.push_back(x);
+    }
+    if (i < 3) {
+      x = downsample(w.down_ds[i], x, h, ww);
+      h /= 2; ww /= 2;
+      skips.push_back(x);
+    }
+  }
+  x = resnet(w.mid_res[0], x, nullptr, h, ww);
+  x = transformer(w.mid_tf, x, h, ww);
+  x = resnet(w.mid_res[1], x, nullptr, h, ww);
+  for (int i = 0; i < 4; ++i) {
+    for (int r = 0; r < 3; ++r) {
+      Buf skip = skips.back();
+      skips.pop_back();
+      x = resnet(w.up_res[i][r], x, &skip, h, ww);  // input = concat [x ; skip], read in place
+      if (i > 0) x = transformer(w.up_tf[i][r], x, h, ww);
+    }
+    if (i < 3) {
+      x = upsample(w.up_us[i], x, h, ww);
+      h *= 2; ww *= 2;
+    }
+  }
+  {
+    const size_t mark = off_;
+    __half* g = alloc_h((size_t)M * 320);
+    gn(x, nullptr, B, HW, w.norm_out, kResEps, true, g);
+    GemmArgs a;
+    a.M = M; a.N = 4; a.K = 9 * 320; a.taps = 9; a.a0 = g; a.cin0 = 320; a.B = B; a.H = H; a.W = W;
+    a.w = w.conv_out.w; a.bias = w.conv_out.b; a.epi = kEpiNchwF32; a.out_f32 = pl_.out; a.rows_per_image = HW;
+    gemm(a, kCatConv3);
+    off_ = mark;
+  }
+  return status_;
+}
+
+// ------------------------------------------------------------------ plans
+Engine::~Engine() {
+  for (auto& kv : plans) {
+    if (kv.second->exec) cudaGraphExecDestroy(kv.second->exec);
+    if (kv.second->graph) cudaGraphDestroy(kv.second->graph);
+    if (kv.second->arena) cudaFree(kv.second->arena);
+  }
+  if (warena) cudaFree(warena);
+  if (op_err) cudaFree(op_err);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
+  if (B < 1 || B > 64 || H < 8 || W < 8 || H > 128 || W > 128 || H % 8 || W % 8 || (W & (W - 1)) || (H & (H - 1)))
+    return fail(SDG_ERR_SHAPE, "unsupported latent shape (B 1..64; H, W powers of two in [8,128])");
+  int st = prepare();
+  if (st) return st;
+  const long key = ((long)mode << 40) | ((long)B << 24) | ((long)H << 12) | W;
+  auto it = plans.find(key);
+  if (it != plans.end()) { *out = it->second.get(); return SDG_OK; }
+  auto pl = std::make_unique<Plan>();
+  pl->B = B; pl->H = H; pl->W = W; pl->mode = mode;
+  {
+    Builder dry(*this, *pl, true, stream);
+    dry.run();
+    pl->arena_bytes = dry.peak();
+  }
+  SDG_CUDA_TRY(cudaSetDevice(device));
+  SDG_CUDA_TRY(cudaMalloc(&pl->arena, pl->arena_bytes));
+  SDG_CUDA_TRY(cudaMemset(pl->arena, 0, pl->arena_bytes));
+  // eager validation pass (sets kernel attributes, surfaces argument errors)
+  {
+    Builder b(*this, *pl, false, stream);
+    st = b.run();
+    if (st) { cudaFree(pl->arena); return st; }
+    pl->launches = b.launches();
+    SDG_CUDA_TRY(cudaStreamSynchronize(stream));
+  }
+  SDG_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  {
+    Builder b(*this, *pl, false, stream);
+    st = b.run();
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(stream, &g);
+    if (st) { if (g) cudaGraphDestroy(g); cudaFree(pl->arena); return st; }
+    if (ce != cudaSuccess) { cudaFree(pl->arena); return fail(SDG_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce)); }
+    pl->graph = g;
+  }
+  SDG_CUDA_TRY(cudaGraphInstantiate(&pl->exec, pl->graph, 0));
+  *out = pl.get();
+  plans[key] = std::move(pl);
+  return SDG_OK;
+}
+
+int Engine::run_plan(Plan* p, cudaStream_t s) {
+  SDG_CUDA_TRY(cudaGraphLaunch(p->exec, s));
+  return SDG_OK;
+}
+
+// Wait for `s` with a deadline (host-side failure detection), then read the
+// plan's device error word.
+static int sync_with_deadline(cudaStream_t s, double seconds) {
+  cudaEvent_t ev;
+  SDG_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  SDG_CUDA_TRY(cudaEventRecord(ev, s));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) { cudaEventDestroy(ev); return fail(SDG_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(q)); }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) {
+      cudaEventDestroy(ev);
+      return fail(SDG_ERR_TIMEOUT, "forward did not complete within the host deadline");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  cudaEventDestroy(ev);
+  return SDG_OK;
+}
+
+int Engine::check_dev_err(Plan* p, cudaStream_t s) {
+  int v = 0;
+  SDG_CUDA_TRY(cudaMemcpyAsync(&v, p->dev_err, 4, cudaMemcpyDeviceToHost, s));
+  SDG_CUDA_TRY(cudaStreamSynchronize(s));
+  if (v != 0) {
+    cudaMemsetAsync(p->dev_err, 0, 4, s);
+    cudaStreamSynchronize(s);
+    char buf[96];
+    snprintf(buf, sizeof buf, "device error word 0x%x (a kernel's bounded wait expired)", v);
+    return fail(SDG_ERR_DEVICE, buf);
+  }
+  return SDG_OK;
+}
+
+}  // namespace sdg
+
+// ====================================================================== C ABI
+using sdg::Engine;
+using sdg::fail;
+
+struct sdg_engine {
+  Engine e;
+};
+
+int sdg_internal_load_dir(sdg_engine* e, const char* dir);  // api_ops.cu
+
+static const double kHostDeadlineS = 60.0;
+
+static int host_forward(sdg_engine* h, const float* latent, const float* tvals, int n_t, const float* context, int B,
+                        int H, int W, float* out, void* stream, int mode) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!latent || !tvals || !context || !out || B <= 0 || (n_t != 1 && n_t != B))
+    return fail(SDG_ERR_ARG, "null pointer or bad n_t");
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, mode, &p);
+  if (st) return st;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+  const size_t L = (size_t)B * 4 * H * W;
+  SDG_CUDA_TRY(cudaMemcpyAsync(p->lat_in, latent, L * 4, cudaMemcpyHostToDevice, s));
+  const int tw = mode == 1 ? 320 : 1;
+  float* tdst = mode == 1 ? p->tproj_in : p->t_in;
+  for (int b = 0; b < B; ++b)
+    SDG_CUDA_TRY(cudaMemcpyAsync(tdst + (size_t)b * tw, tvals + (size_t)(n_t == 1 ? 0 : b) * tw, tw * 4,
+                                 cudaMemcpyHostToDevice, s));
+  SDG_CUDA_TRY(cudaMemcpyAsync(p->ctx_in, context, (size_t)B * 77 * 768 * 4, cudaMemcpyHostToDevice, s));
+  st = e.run_plan(p, s);
+  if (st) return st;
+  SDG_CUDA_TRY(cudaMemcpyAsync(out, p->out, L * 4, cudaMemcpyDeviceToHost, s));
+  st = sdg::sync_with_deadline(s, kHostDeadlineS);
+  if (st) return st;
+  return e.check_dev_err(p, s);
+}
+
+extern "C" {
+
+SDG_API int sdg_init(int device, const char* weights_dir, sdg_engine** out) {
+  if (!out) return fail(SDG_ERR_ARG, "out is null");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t ce = cudaGetDeviceCount(&n);
+  if (ce != cudaSuccess || device < 0 || device >= n)
+    return fail(SDG_ERR_CUDA, std::string("no CUDA device ") + std::to_string(device) + ": " + cudaGetErrorString(ce));
+  cudaSetDevice(device);
+  auto* h = new sdg_engine();
+  h->e.device = device;
+  if (cudaStreamCreateWithFlags(&h->e.stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&h->e.op_err, 256) != cudaSuccess || cudaMemset(h->e.op_err, 0, 256) != cudaSuccess) {
+    delete h;
+    return fail(SDG_ERR_CUDA, "stream / error word allocation failed");
+  }
+  if (weights_dir) {
+    int st = sdg_load_dir(h, weights_dir);
+    if (st) { delete h; return st; }
+  }
+  *out = h;
+  return SDG_OK;
+}
+
+SDG_API int sdg_upload_weight(sdg_engine* h, const char* key, const uint16_t* fp16, const int64_t* shape, int ndim) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!key || !fp16 || !shape || ndim <= 0 || ndim > 4) return fail(SDG_ERR_ARG, "bad weight arguments");
+  if (h->e.prepared) return fail(SDG_ERR_ARG, "weights already prepared; create a new engine to change them");
+  size_t n = 1;
+  for (int i = 0; i < ndim; ++i) {
+    if (shape[i] <= 0) return fail(SDG_ERR_ARG, "bad shape");
+    n *= (size_t)shape[i];
+  }
+  sdg::HostWeight& hw = h->e.host[key];
+  hw.data.assign(fp16, fp16 + n);
+  hw.shape.assign(shape, shape + ndim);
+  return SDG_OK;
+}
+
+SDG_API int sdg_load_dir(sdg_engine* h, const char* dir) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!dir) return fail(SDG_ERR_ARG, "dir is null");
+  return sdg_internal_load_dir(h, dir);
+}
+
+SDG_API int sdg_prepare(sdg_engine* h) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  cudaSetDevice(h->e.device);
+  return h->e.prepare();
+}
+
+SDG_API int sdg_release(sdg_engine* h) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  cudaSetDevice(h->e.device);
+  cudaStreamSynchronize(h->e.stream);
+  delete h;
+  return SDG_OK;
+}
+
+SDG_API int sdg_last_error(char* buf, int n) {
+  if (!buf || n <= 0) return SDG_ERR_ARG;
+  snprintf(buf, (size_t)n, "%s", sdg::g_last_error.c_str());
+  return SDG_OK;
+}
+
+SDG_API int sdg_unet_forward(sdg_engine* h, const float* latent, const float* timesteps, int n_t, const float* context,
+                             int B, int H, int W, float* out, void* stream) {
+  return host_forward(h, latent, timesteps, n_t, context, B, H, W, out, stream, 0);
+}
+
+SDG_API int sdg_unet_forward_tproj(sdg_engine* h, const float* latent, const float* temb_proj, int n_t,
+                                   const float* context, int B, int H, int W, float* out, void* stream) {
+  return host_forward(h, latent, temb_proj, n_t, context, B, H, W, out, stream, 1);
+}
+
+SDG_API int sdg_unet_forward_device(sdg_engine* h, const float* latent, const float* timesteps, int n_t,
+                                    const float* context, int B, int H, int W, float* out, void* stream) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!latent || !timesteps || !context || !out || B <= 0 || (n_t != 1 && n_t != B))
+    return fail(SDG_ERR_ARG, "null pointer or bad n_t");
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return st;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+  const size_t L = (size_t)B * 4 * H * W;
+  SDG_CUDA_TRY(cudaMemcpyAsync(p->lat_in, latent, L * 4, cudaMemcpyDeviceToDevice, s));
+  for (int b = 0; b < B; ++b)
+    SDG_CUDA_TRY(cudaMemcpyAsync(p->t_in + b, timesteps + (n_t == 1 ? 0 : b), 4, cudaMemcpyDeviceToDevice, s));
+  SDG_CUDA_TRY(cudaMemcpyAsync(p->ctx_in, context, (size_t)B * 77 * 768 * 4, cudaMemcpyDeviceToDevice, s));
+  st = e.run_plan(p, s);
+  if (st) return st;
+  SDG_CUDA_TRY(cudaMemcpyAsync(out, p->out, L * 4, cudaMemcpyDeviceToDevice, s));
+  return SDG_OK;
+}
+
+SDG_API int sdg_unet_forward_cfg(sdg_engine* h, const float* latent, float timestep, const float* cond,
+                                 const float* uncond, int H, int W, float* out2) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!latent || !cond || !uncond || !out2) return fail(SDG_ERR_ARG, "null pointer");
+  const size_t L = (size_t)4 * H * W, CT = (size_t)77 * 768;
+  std::vector<float> lat2(2 * L), ctx2(2 * CT);
+  memcpy(lat2.data(), latent, L * 4);
+  memcpy(lat2.data() + L, latent, L * 4);
+  memcpy(ctx2.data(), cond, CT * 4);
+  memcpy(ctx2.data() + CT, uncond, CT * 4);
+  return host_forward(h, lat2.data(), &timestep, 1, ctx2.data(), 2, H, W, out2, nullptr, 0);
+}
+
+// LCM scheduler constants, restating LcmScheduler.kt:25-54 (diffusers
+// LCMScheduler: scaled-linear betas 0.00085..0.012 over 1000 steps, 50 original
+// inference steps, timestep_scaling 10, sigma_data 0.5), in double precision.
+static void lcm_schedule(int steps, std::vector<int>& ts, std::vector<double>& ac) {
+  ac.resize(1000);
+  double acc = 1.0;
+  const double b0 = sqrt(0.00085), b1 = sqrt(0.012);
+  for (int i = 0; i < 1000; ++i) {
+    const double b = pow(b0 + (b1 - b0) * i / 999.0, 2.0);
+    acc *= 1.0 - b;
+    ac[i] = acc;
+  }
+  ts.resize(steps);
+  for (int i = 0; i < steps; ++i) {
+    const int idx = (int)floor((double)i * 50 / steps);
+    ts[i] = (49 - idx + 1) * 20 - 1;  // reversed [19, 39, ..., 999]
+  }
+}
+
+SDG_API int sdg_lcm_denoise(sdg_engine* h, const float* latents, const float* cond, const float* uncond,
+                            const float* step_noise, int n_img, int H, int W, int steps, float cfg, float* out) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (!latents || !cond || !uncond || !out || n_img <= 0 || n_img > 32 || steps <= 0 || steps > 50 ||
+      (steps > 1 && !step_noise))
+    return fail(SDG_ERR_ARG, "lcm: bad arguments (n_img 1..32, steps 1..50)");
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  const int B = 2 * n_img;
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return st;
+  cudaStream_t s = e.stream;
+  const size_t L = (size_t)4 * H * W, CT = (size_t)77 * 768;
+  // device state: latents [n_img, L] and the step noise [steps-1, n_img, L]
+  float* dlat = nullptr;
+  float* dnoise = nullptr;
+  const size_t nn = steps > 1 ? (size_t)(steps - 1) * n_img * L : 1;
+  SDG_CUDA_TRY(cudaMallocAsync(&dlat, (size_t)n_img * L * 4, s));
+  SDG_CUDA_TRY(cudaMallocAsync(&dnoise, nn * 4, s));
+  std::vector<float> pair((size_t)B * L), ctx((size_t)B * CT);
+  for (int i = 0; i < n_img; ++i) {
+    memcpy(&pair[(size_t)(2 * i) * L], latents + (size_t)i * L, L * 4);
+    memcpy(&pair[(size_t)(2 * i + 1) * L], latents + (size_t)i * L, L * 4);
+    memcpy(&ctx[(size_t)(2 * i) * CT], cond + (size_t)i * CT, CT * 4);
+    memcpy(&ctx[(size_t)(2 * i + 1) * CT], uncond + (size_t)i * CT, CT * 4);
+  }
+  int rc = SDG_OK;
+  auto run = [&]() -> int {
+    SDG_CUDA_TRY(cudaMemcpyAsync(dlat, latents, (size_t)n_img * L * 4, cudaMemcpyHostToDevice, s));
+    if (steps > 1) SDG_CUDA_TRY(cudaMemcpyAsync(dnoise, step_noise, nn * 4, cudaMemcpyHostToDevice, s));
+    SDG_CUDA_TRY(cudaMemcpyAsync(p->lat_in, pair.data(), pair.size() * 4, cudaMemcpyHostToDevice, s));
+    SDG_CUDA_TRY(cudaMemcpyAsync(p->ctx_in, ctx.data(), ctx.size() * 4, cudaMemcpyHostToDevice, s));
+    std::vector<int> ts;
+    std::vector<double> ac;
+    lcm_schedule(steps, ts, ac);
+    std::vector<float> tv(B);
+    for (int i = 0; i < steps; ++i) {
+      const int t = ts[i];
+      for (int b = 0; b < B; ++b) tv[b] = (float)t;
+      SDG_CUDA_TRY(cudaMemcpyAsync(p->t_in, tv.data(), B * 4, cudaMemcpyHostToDevice, s));
+      int r = e.run_plan(p, s);
+      if (r) return r;
+      const double aT = ac[t], bT = 1.0 - aT, stt = t * 10.0, sd2 = 0.25;
+      const double c_skip = sd2 / (stt * stt + sd2), c_out = stt / sqrt(stt * stt + sd2);
+      const bool last = i == steps - 1;
+      const double aP = last ? 1.0 : ac[ts[i + 1]];
+      SDG_CUDA_TRY(sdg::launch_cfg_lcm(p->out, dlat, last ? nullptr : dnoise + (size_t)i * n_img * L, n_img, (int)L, cfg,
+                                       c_skip, c_out, sqrt(aT), sqrt(bT), sqrt(aP), sqrt(1.0 - aP), last ? 1 : 0,
+                                       last ? nullptr : p->lat_in, s));
+      // the copy of pair/ctx/timesteps above came from pageable host memory;
+      // tv is reused, so make the copy of this step complete before rewriting it
+      SDG_CUDA_TRY(cudaStreamSynchronize(s));
+    }
+    SDG_CUDA_TRY(cudaMemcpyAsync(out, dlat, (size_t)n_img * L * 4, cudaMemcpyDeviceToHost, s));
+    int r = sdg::sync_with_deadline(s, kHostDeadlineS * steps);
+    if (r) return r;
+    return e.check_dev_err(p, s);
+  };
+  rc = run();
+  cudaFreeAsync(dlat, s);
+  cudaFreeAsync(dnoise, s);
+  cudaStreamSynchronize(s);
+  return rc;
+}
+
+SDG_API int sdg_forward_launches(sdg_engine* h, int B, int H, int W) {
+  if (!h) return -SDG_ERR_NOT_INIT;
+  for (auto& kv : h->e.plans)
+    if (kv.second->B == B && kv.second->H == H && kv.second->W == W) return kv.second->launches;
+  return -SDG_ERR_ARG;
+}
+
+SDG_API int sdg_profile(sdg_engine* h, int B, int H, int W, sdg_profile_row* rows, int cap) {
+  if (!h) return -SDG_ERR_NOT_INIT;
+  if (!rows || cap <= 0) return -SDG_ERR_ARG;
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return -st;
+  sdg::Builder b(e, *p, false, e.stream);
+  b.profile = true;
+  st = b.run();
+  if (cudaStreamSynchronize(e.stream) != cudaSuccess || st) return -SDG_ERR_CUDA;
+  double ms[sdg::kCatCount] = {0};
+  int cnt[sdg::kCatCount] = {0};
+  for (auto& pr : b.prof) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, pr.second.first, pr.second.second);
+    ms[pr.first] += t;
+    cnt[pr.first]++;
+    cudaEventDestroy(pr.second.first);
+    cudaEventDestroy(pr.second.second);
+  }
+  int n = 0;
+  for (int c = 0; c < sdg::kCatCount && n < cap; ++c) {
+    if (!cnt[c]) continue;
+    snprintf(rows[n].name, sizeof rows[n].name, "%s", sdg::kCatName[c]);
+    rows[n].ms = ms[c];
+    rows[n].launches = cnt[c];
+    ++n;
+  }
+  return n;
+}
+
+}  // extern "C"

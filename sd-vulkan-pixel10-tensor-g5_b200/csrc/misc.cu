@@ -1,0 +1,263 @@
+// misc.cu — small bandwidth kernels around the tensor-core path:
+// time embedding (VulkanUnetPipeline.kt:36-46 sinusoid, computed in fp64),
+// small-M GEMV (time MLP vk_engine.cpp:716-717, per-ResNet time_emb_proj
+// :627-630, batched into one launch), im2col for the stride-2 downsample and
+// the 4-channel conv_in, nearest 2x upsample (upsample_f32.comp), channel
+// concat (vk_engine.cpp:677-688), add, and the fused CFG-combine + LCM step
+// (VulkanUnetPipeline.kt:86, LcmScheduler.kt:56-82).
+#include <cmath>
+
+#include "sdg_kernels.h"
+#include "sdg_ptx.cuh"
+
+namespace sdg {
+namespace {
+
+__global__ void time_embedding_kernel(const float* t, int n_t, int B, const float* tin, float* out) {
+  const int b = blockIdx.x;
+  const int i = threadIdx.x;  // 0..159
+  if (i >= 160) return;
+  float* o = out + (size_t)b * 320;
+  if (tin) {
+    const float* src = tin + (size_t)(n_t == 1 ? 0 : b) * 320;
+    o[i] = src[i];
+    o[160 + i] = src[160 + i];
+    return;
+  }
+  const double tv = (double)t[n_t == 1 ? 0 : b];
+  const double freq = exp(-log(10000.0) * (double)i / 160.0);
+  const double arg = tv * freq;
+  o[i] = (float)cos(arg);
+  o[160 + i] = (float)sin(arg);
+}
+
+constexpr int kGemvMaxM = 8;
+constexpr int kGemvMaxK = 1280;
+
+__global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, int M, int K, const __half* __restrict__ w,
+                                                   const float* __restrict__ bias, int N, int act_in, int act_out,
+                                                   float* __restrict__ y, int ldy) {
+  __shared__ float xs[kGemvMaxM * kGemvMaxK];
+  for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
+    const float v = x[i];
+    xs[i] = act_in ? silu_f(v) : v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (n >= N) return;
+  const __half* wr = w + (size_t)n * K;
+  float acc[kGemvMaxM];
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) acc[m] = 0.f;
+  for (int k0 = lane * 8; k0 < K; k0 += 256) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(wr + k0));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    float wf[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __half22float2(h[e]);
+      wf[2 * e] = f.x;
+      wf[2 * e + 1] = f.y;
+    }
+#pragma unroll
+    for (int m = 0; m < kGemvMaxM; ++m) {
+      if (m < M) {
+        const float* xr = xs + m * K + k0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m] += wf[e] * xr[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) {
+    float v = acc[m];
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && m < M) {
+      v += bias ? bias[n] : 0.f;
+      if (act_out) v = silu_f(v);
+      y[(size_t)m * ldy + n] = v;
+    }
+  }
+}
+
+// col[(b*Ho+oy)*Wo+ox, tap*C + c] = x[b, oy*s+ky-1, ox*s+kx-1, c] (0 outside)
+__global__ void im2col3x3_kernel(const __half* __restrict__ x, int B, int H, int W, int C, int stride, int Ho, int Wo,
+                                 int Kpad, __half* __restrict__ col) {
+  const int nvec = C / 8;
+  const size_t total = (size_t)B * Ho * Wo * 9 * nvec;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % nvec);
+    const size_t r = i / nvec;
+    const int tap = (int)(r % 9);
+    const size_t pix = r / 9;
+    const int ox = (int)(pix % Wo);
+    const int oy = (int)((pix / Wo) % Ho);
+    const int b = (int)(pix / ((size_t)Wo * Ho));
+    const int iy = oy * stride + tap / 3 - 1, ix = ox * stride + tap % 3 - 1;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W) u = *reinterpret_cast<const uint4*>(x + (((size_t)b * H + iy) * W + ix) * C + v * 8);
+    *reinterpret_cast<uint4*>(col + pix * Kpad + tap * C + v * 8) = u;
+  }
+}
+
+// conv_in operand: lat NCHW fp32 [B,Cl,H,W] -> col [B*H*W, Kpad], K index = tap*Cl + c, zero padded.
+__global__ void latent_im2col_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W, int Kpad,
+                                     __half* __restrict__ col) {
+  const size_t total = (size_t)B * H * W * Kpad;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i % Kpad);
+    const size_t pix = i / Kpad;
+    float v = 0.f;
+    if (k < 9 * Cl) {
+      const int tap = k / Cl, c = k % Cl;
+      const int x = (int)(pix % W), y = (int)((pix / W) % H), b = (int)(pix / ((size_t)W * H));
+      const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = lat[(((size_t)b * Cl + c) * H + iy) * W + ix];
+    }
+    col[i] = __float2half_rn(v);
+  }
+}
+
+__global__ void upsample2x_kernel(const __half* __restrict__ x, int B, int H, int W, int C, __half* __restrict__ y) {
+  const int nvec = C / 8;
+  const int Ho = 2 * H, Wo = 2 * W;
+  const size_t total = (size_t)B * Ho * Wo * nvec;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % nvec);
+    const size_t pix = i / nvec;
+    const int ox = (int)(pix % Wo), oy = (int)((pix / Wo) % Ho), b = (int)(pix / ((size_t)Wo * Ho));
+    const uint4 u = *reinterpret_cast<const uint4*>(x + (((size_t)b * H + oy / 2) * W + ox / 2) * C + v * 8);
+    *reinterpret_cast<uint4*>(y + pix * C + v * 8) = u;
+  }
+}
+
+__global__ void concat_kernel(const __half* __restrict__ a, int Ca, const __half* __restrict__ b, int Cb, int rows,
+                              __half* __restrict__ y) {
+  const int C = Ca + Cb, nvec = C / 8;
+  const size_t total = (size_t)rows * nvec;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % nvec) * 8;
+    const size_t r = i / nvec;
+    const uint4 u = c < Ca ? *reinterpret_cast<const uint4*>(a + r * Ca + c) : *reinterpret_cast<const uint4*>(b + r * Cb + (c - Ca));
+    *reinterpret_cast<uint4*>(y + r * C + c) = u;
+  }
+}
+
+__global__ void add_kernel(const __half2* __restrict__ a, const __half2* __restrict__ b, size_t n2, __half2* __restrict__ y) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n2; i += (size_t)gridDim.x * blockDim.x) {
+    const float2 fa = __half22float2(a[i]), fb = __half22float2(b[i]);
+    y[i] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, size_t n, __half* __restrict__ y) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+
+// eps2: [n_img, 2, L] (cond then uncond per image); latents [n_img, L] fp32.
+// eps = uncond + cfg*(cond-uncond); LCM step (LcmScheduler.kt:68-80, fp64 math
+// like the Kotlin reference); lat_pair[img, 0|1, :] = new latents (input of
+// the next batch-CFG forward).
+__global__ void cfg_lcm_kernel(const float* __restrict__ eps2, float* __restrict__ lat, const float* __restrict__ noise,
+                               int n_img, int L, float cfg, double c_skip, double c_out, double sa, double sb,
+                               double sap, double sbp, int last, float* __restrict__ lat_pair) {
+  const size_t total = (size_t)n_img * L;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t img = i / L, j = i % L;
+    const float ec = eps2[(img * 2 + 0) * L + j];
+    const float eu = eps2[(img * 2 + 1) * L + j];
+    const float e = eu + cfg * (ec - eu);
+    const double x = (double)lat[i];
+    const double x0 = (x - sb * (double)e) / sa;
+    const double den = c_out * x0 + c_skip * x;
+    const float nv = last ? (float)den : (float)(sap * den + sbp * (double)noise[i]);
+    lat[i] = nv;
+    if (lat_pair) {
+      lat_pair[(img * 2 + 0) * L + j] = nv;
+      lat_pair[(img * 2 + 1) * L + j] = nv;
+    }
+  }
+}
+
+inline int grid_for(size_t n, int threads = 256) {
+  size_t g = (n + threads - 1) / threads;
+  const size_t cap = (size_t)num_sms() * 16;
+  if (g > cap) g = cap;
+  return (int)(g ? g : 1);
+}
+
+}  // namespace
+
+cudaError_t launch_time_embedding(const float* t, int n_t, int B, const float* tin, float* out320, cudaStream_t s) {
+  if (B <= 0 || (n_t != 1 && n_t != B)) return cudaErrorInvalidValue;
+  time_embedding_kernel<<<B, 160, 0, s>>>(t, n_t, B, tin, out320);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const float* bias, int N, int act_in, int act_out,
+                        float* y, int ldy, cudaStream_t s) {
+  if (M <= 0 || K <= 0 || K > kGemvMaxK || K % 8) return cudaErrorInvalidValue;
+  const int blocks = (N + 7) / 8;
+  for (int m0 = 0; m0 < M; m0 += kGemvMaxM) {  // rows in chunks of kGemvMaxM
+    const int mc = M - m0 < kGemvMaxM ? M - m0 : kGemvMaxM;
+    gemv_kernel<<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, w, bias, N, act_in, act_out, y + (size_t)m0 * ldy, ldy);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int stride, int Kpad, __half* col,
+                             cudaStream_t s) {
+  if (C % 8 || Kpad < 9 * C) return cudaErrorInvalidValue;
+  const int Ho = (H + 2 - 3) / stride + 1, Wo = (W + 2 - 3) / stride + 1;
+  const size_t total = (size_t)B * Ho * Wo * 9 * (C / 8);
+  im2col3x3_kernel<<<grid_for(total), 256, 0, s>>>(x, B, H, W, C, stride, Ho, Wo, Kpad, col);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_latent_im2col(const float* lat, int B, int Cl, int H, int W, int Kpad, __half* col, cudaStream_t s) {
+  if (Kpad < 9 * Cl) return cudaErrorInvalidValue;
+  const size_t total = (size_t)B * H * W * Kpad;
+  latent_im2col_kernel<<<grid_for(total), 256, 0, s>>>(lat, B, Cl, H, W, Kpad, col);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_upsample2x(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t s) {
+  if (C % 8) return cudaErrorInvalidValue;
+  const size_t total = (size_t)B * 4 * H * W * (C / 8);
+  upsample2x_kernel<<<grid_for(total), 256, 0, s>>>(x, B, H, W, C, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_concat(const __half* a, int Ca, const __half* b, int Cb, int rows, __half* y, cudaStream_t s) {
+  if (Ca % 8 || Cb % 8) return cudaErrorInvalidValue;
+  const size_t total = (size_t)rows * ((Ca + Cb) / 8);
+  concat_kernel<<<grid_for(total), 256, 0, s>>>(a, Ca, b, Cb, rows, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(const __half* a, const __half* b, size_t n, __half* y, cudaStream_t s) {
+  if (n % 2) return cudaErrorInvalidValue;
+  add_kernel<<<grid_for(n / 2), 256, 0, s>>>(reinterpret_cast<const __half2*>(a), reinterpret_cast<const __half2*>(b), n / 2,
+                                             reinterpret_cast<__half2*>(y));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_f16(const float* x, size_t n, __half* y, cudaStream_t s) {
+  f32_to_f16_kernel<<<grid_for(n), 256, 0, s>>>(x, n, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cfg_lcm(const float* eps2, float* latents, const float* noise, int n_img, int L, float cfg,
+                           double c_skip, double c_out, double sa, double sb, double sap, double sbp, int last,
+                           float* lat_pair, cudaStream_t s) {
+  const size_t total = (size_t)n_img * L;
+  cfg_lcm_kernel<<<grid_for(total), 256, 0, s>>>(eps2, latents, noise, n_img, L, cfg, c_skip, c_out, sa, sb, sap, sbp,
+                                                 last, lat_pair);
+  return cudaGetLastError();
+}
+
+}  // namespace sdg

@@ -1,0 +1,105 @@
+// sdg_kernels.h — host-side launch interface of the engine's CUDA kernels.
+// All activations are fp16 NHWC ([B, H, W, C] == token-major [B*H*W, C]).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sdg {
+
+enum EpiMode : int {
+  kEpiPlain = 0,    // out[m, n] fp16 (row stride ld_out)
+  kEpiGeglu = 1,    // tile holds [a | gate] column halves; out[m, n/2-space] = a * gelu(gate)
+  kEpiHeads = 2,    // scatter into padded per-head layout [B*heads, S, dp] (Q/K/V for attention)
+  kEpiNchwF32 = 3,  // out_f32[b, n, p] fp32 (final conv_out)
+};
+
+// One GEMM / implicit-GEMM convolution: D[M,N] = A[M,K] * W[N,K]^T with the
+// fused epilogue  act(D + bias[n] + rowbias[img(m), n] + residual[m, n]).
+// A is either a row-major [M, K] activation matrix (taps == 1) or, for a
+// stride-1 pad-1 3x3 convolution (taps == 9), gathered on the fly from the
+// NHWC input by 4D TMA boxes shifted per tap (out-of-range rows/columns read
+// as zero == the convolution's zero padding). A may come from two sources
+// (channel concat [src0 ; src1]): K-chunks with channel < cin0 read src0.
+struct GemmArgs {
+  int M = 0, N = 0, K = 0;
+  int taps = 1;
+  const __half* a0 = nullptr;  // source 0: [M, cin0] (taps 1) or NHWC [B,H,W,cin0] (taps 9)
+  const __half* a1 = nullptr;  // source 1 (concat) or null
+  int cin0 = 0, cin1 = 0;      // channels per tap from each source
+  int lda0 = 0, lda1 = 0;      // row strides (elements) for taps == 1 (default cin)
+  int B = 1, H = 1, W = 1;     // conv geometry (taps == 9)
+  const __half* w = nullptr;   // [N, K] K-major (conv: [Co][tap][Cin])
+  // epilogue
+  int epi = kEpiPlain;
+  int act = 0;                      // 0 none, 1 SiLU
+  const float* bias = nullptr;      // [N]
+  const float* rowbias = nullptr;   // [images, rowbias_ld]
+  int rowbias_ld = 0;
+  int rows_per_image = 1;           // m / rows_per_image = image index (rowbias, heads, nchw)
+  const __half* residual = nullptr; // [M, ld_res]
+  int ld_res = 0;
+  __half* out = nullptr;
+  int ld_out = 0;
+  float* out_f32 = nullptr;
+  __half* head_out[3] = {nullptr, nullptr, nullptr};
+  int head_C = 0, heads = 0, head_d = 0, head_dp = 0;
+  int head_vt = -1;                 // index of the output stored transposed [BH, d16, head_spad]
+  int head_d16 = 0, head_spad = 0;
+  int bn = 0;                       // tile N (0 = choose)
+};
+
+cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s);
+
+// GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
+// tensors. stats: scratch of B*(C0+C1)*2 floats, zeroed by the caller.
+struct GroupNormArgs {
+  const __half* x0 = nullptr; const __half* x1 = nullptr;
+  int C0 = 0, C1 = 0, B = 1, HW = 1, groups = 32;
+  const float* gamma = nullptr; const float* beta = nullptr;
+  float eps = 1e-5f; int silu = 1;
+  __half* y = nullptr;
+  float* stats = nullptr;
+};
+cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s);
+
+cudaError_t launch_layernorm(const __half* x, int M, int C, const float* gamma, const float* beta, float eps,
+                             __half* y, cudaStream_t s);
+
+// Flash attention over padded per-head layouts: q [BH, Sq, dp], k [BH, Sk, dp]
+// (dp = d rounded up to 64), v transposed [BH, d16, vt_ld] (d16 = d rounded up
+// to 16, vt_ld >= Sk, multiple of 8); fp16, zero in every padding column/row.
+// out o[(b*Sq + i)*ld_o + h*d + j] fp16.
+struct AttnArgs {
+  const __half* q = nullptr; const __half* k = nullptr; const __half* v = nullptr;
+  int BH = 0, heads = 0, Sq = 0, Sk = 0, d = 0, dp = 0, d16 = 0, vt_ld = 0;
+  __half* o = nullptr; int ld_o = 0;
+  float scale = 0.f;
+};
+cudaError_t launch_attention(const AttnArgs& a, int* dev_err, cudaStream_t s);
+
+// small kernels (sdg_misc.cu)
+cudaError_t launch_time_embedding(const float* timesteps, int n_t, int B, const float* temb_proj_in, float* out320,
+                                  cudaStream_t s);
+// y[m, n] = act(x[m,:] . w[n,:] + bias[n]) for small M (<= 8); x fp32 [M,K], w fp16 [N,K], y fp32.
+cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const float* bias, int N, int act_in,
+                        int act_out, float* y, int ldy, cudaStream_t s);
+cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int stride, int Kpad, __half* col,
+                             cudaStream_t s);
+cudaError_t launch_latent_im2col(const float* lat_nchw, int B, int C, int H, int W, int Kpad, __half* col,
+                                 cudaStream_t s);
+cudaError_t launch_upsample2x(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t s);
+cudaError_t launch_concat(const __half* a, int Ca, const __half* b, int Cb, int rows, __half* y, cudaStream_t s);
+cudaError_t launch_add(const __half* a, const __half* b, size_t n, __half* y, cudaStream_t s);
+cudaError_t launch_f32_to_f16(const float* x, size_t n, __half* y, cudaStream_t s);
+// Fused CFG combine + LCM step over n_img images of L latent elements.
+// eps2 [n_img, 2, L] (cond, uncond), latents [n_img, L] updated in place,
+// lat_pair [n_img, 2, L] (optional) receives the new latents twice.
+cudaError_t launch_cfg_lcm(const float* eps2, float* latents, const float* noise, int n_img, int L, float cfg,
+                           double c_skip, double c_out, double sqrt_alpha, double sqrt_beta, double sqrt_alpha_prev,
+                           double sqrt_beta_prev, int last, float* lat_pair, cudaStream_t s);
+
+int num_sms();
+
+}  // namespace sdg
