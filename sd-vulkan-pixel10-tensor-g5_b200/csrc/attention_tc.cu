@@ -40,6 +40,8 @@ struct AttnCfg {
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
   static constexpr int kThreads = 64 + 128 * NQT;
   static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)NQT * kPTile + 1024;
+  static_assert(kSmem <= 232448, "attention tile configuration exceeds 227 KB of shared memory");
+  static_assert(kTmemNeed <= 512, "attention tile configuration exceeds TMEM");
 };
 
 struct AttnDev {
@@ -327,7 +329,7 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
   switch (a.d16) {
     case 48: return launch_cfg<AttnCfg<64, 128, 2, 48>>(a, err, s);
     case 64: return launch_cfg<AttnCfg<64, 128, 2, 64>>(a, err, s);
-    case 80: return launch_cfg<AttnCfg<128, 128, 2, 80>>(a, err, s);
+    case 80: return launch_cfg<AttnCfg<128, 128, 1, 80>>(a, err, s);
     case 160: return launch_cfg<AttnCfg<192, 64, 1, 160>>(a, err, s);
     default: return cudaErrorInvalidValue;
   }

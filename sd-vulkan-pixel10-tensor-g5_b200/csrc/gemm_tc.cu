@@ -56,6 +56,7 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = (2 * kAccStride) < 32 ? 32 : 2 * kAccStride;
   static constexpr int kChunk = BN >= 32 ? 32 : 16;
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
+  static_assert(kSmem <= 232448, "GEMM tile configuration exceeds 227 KB of shared memory");
 };
 
 __device__ __forceinline__ void store_row_chunk(__half* dst, const float* v, int n) {
