@@ -1,0 +1,299 @@
+"""Benchmark of the SD1.5 UNet forward on B200 (driver contract).
+
+One step = one UNet forward at BASELINE config 0: B=2 (a CFG cond/uncond
+pair), 64x64 latent, 77x768 context, timestep 999, seeded default-init fp16
+weights, synthetic seeded inputs. Each rank holds a full weight copy and runs
+its own B=2 forwards (data parallel by batch, no collective on the hot path);
+`value` is whole-job forwards/s over all ranks (max-over-ranks device time).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank binds cuda:LOCAL_RANK; NCCL is used only for the
+barrier and the max-over-ranks reduction of the timing.
+The reference arm (--impl reference) times the CPU oracle port of the
+reference forward on the host cores (the reference's own Vulkan engine
+cannot run on this box: no graphics stack).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "UNet fwd/s (B=2 CFG, 64×64 latent) at 1/2/4/8 B200; % dense-fp16 tensor peak"
+UNIT = "fwd/s"
+B, H, W = 2, 64, 64
+FLOPS_PER_FWD = 1.606e12          # algorithmic FLOPs per B=2 64x64 forward (direct-conv count)
+L2_FLUSH_BYTES = 256 << 20        # > 126 MB L2
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=lambda: self.lines.extend(iter(self.proc.stdout.readline, "")), daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_engine(sdg, device):
+    from oracle import weights as Wt
+    w = Wt.make_weights(0)
+    eng = sdg.Engine(device)
+    eng.upload_weights(Wt.iter_reference_blobs(w))
+    eng.prepare()
+    return eng, w
+
+
+def cpu_oracle_forward_rate(w, threads, budget_s=30.0):
+    """Time the fp32 oracle forward (config 0) on host cores; returns (fwd/s, sample str)."""
+    import torch
+    from oracle import unet_ref as R
+    from oracle import weights as Wt
+    torch.set_num_threads(threads)
+    lat, t, ctx = Wt.make_inputs(B, H, W, seed=0)
+    wf = {k: v.float() for k, v in w.items()}   # fp16-rounded weights held in fp32
+    n, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        while True:
+            R.unet_forward(lat, t, ctx, wf)
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s * 0.5 or n >= 2:
+                break
+    return n / el, f"{n} full B=2 64x64 fp32 oracle forward(s), {el:.1f} s"
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from oracle import weights as Wt
+    from oracle import unet_ref as R
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = Wt.make_weights(0)
+    wf = {k: v.float() for k, v in w.items()}
+    lat, t, ctx = Wt.make_inputs(B, H, W, seed=0)
+    budget = float(os.environ.get("SDG_REF_BUDGET_S", "150"))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        R.unet_forward(lat, t, ctx, wf)                      # one warm-up forward
+        per = time.perf_counter() - t0
+        steps = max(1, min(args.steps, int(budget / max(per, 1e-3))))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            R.unet_forward(lat, t, ctx, wf)
+        el = time.perf_counter() - t0
+    v = steps / el
+    sample = f"{steps} of {args.steps} requested steps (1 warm-up), each a full B=2 64x64 fp32 forward"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": 1, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 0)",
+        "config": config_dict(args.gpus),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference Vulkan engine unavailable on this box (no graphics stack); timed arm = CPU restatement "
+                "of vk_engine.cpp runGraph (oracle/unet_ref.py) in PyTorch fp32 on all host threads",
+    }))
+    return 0
+
+
+def config_dict(n):
+    return {"workload": "SD1.5 UNet forward, B=2 CFG pair, 64x64 latent, 77x768 context, t=999 (BASELINE config 0)",
+            "global_batch": 2 * n, "latent": [H, W], "context": [77, 768], "parallelism": f"dp{n} (weights replicated)",
+            "l2": "256 MB L2 flush (memset) between timed steps, outside the timed events; weights 1.72 GB > L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    sdg = importlib.import_module("sd-vulkan-pixel10-tensor-g5_b200")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    eng, wts = make_engine(sdg, local)
+    from oracle import weights as Wt
+    lat, t, ctx = Wt.make_inputs(B, H, W, seed=rank)
+    d_lat, d_t, d_ctx = lat.to(dev), t.to(dev), ctx.to(dev)
+    d_out = torch.empty_like(d_lat)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        eng.forward_device(d_lat, d_t, d_ctx, d_out, stream.cuda_stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K device-resident forwards, CUDA events per step, L2 flushed between steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t_max = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    dev_ms = float(t_max.item())
+    ms_per_step = dev_ms / args.steps
+    value = world * args.steps / (dev_ms / 1000.0)
+
+    # ---- e2e: the public host API (pinned host inputs, H2D + forward + D2H per step)
+    p_lat = torch.empty(lat.shape, dtype=torch.float32).pin_memory()
+    p_ctx = torch.empty(ctx.shape, dtype=torch.float32).pin_memory()
+    p_t = torch.empty(t.shape, dtype=torch.float32).pin_memory()
+    p_lat.copy_(lat); p_ctx.copy_(ctx); p_t.copy_(t)
+    n_lat, n_ctx, n_t = p_lat.numpy(), p_ctx.numpy(), p_t.numpy()
+    for _ in range(2):
+        eng.forward(n_lat, n_t, n_ctx)
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(5, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        out_host = eng.forward(n_lat, n_t, n_ctx)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * e2e_steps / float(te.item())
+    h2d = n_lat.nbytes + n_ctx.nbytes + n_t.nbytes
+    d2h = out_host.nbytes
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM / implicit conv), per-launch CUDA events
+    prof = eng.profile(B, H, W)
+    gemm_ms = sum(prof[c][0] for c in ("CONV3", "GEMM") if c in prof)
+    gemm_fl = sum(prof[c][2] for c in ("CONV3", "GEMM") if c in prof)
+    gemm_n = sum(prof[c][1] for c in ("CONV3", "GEMM") if c in prof)
+    hbm, tc_burst, tc_sust, src = peaks()
+    achieved = gemm_fl / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel (conv3x3 implicit GEMM + linears)",
+                "achieved": achieved, "peak": tc_burst, "unit": "TFLOP/s",
+                "frac": (achieved / tc_burst) if achieved else None, "peak_source": f"{src} bf16_tflops (burst)",
+                "traffic": None, "launches_per_fwd": gemm_n, "flops_per_fwd": gemm_fl,
+                "whole_forward_tflops": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12,
+                "whole_forward_frac_of_sustained": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_sust,
+                "categories_ms": {k: round(v[0], 4) for k, v in prof.items()}}
+    gn = prof.get("GN")
+    if gn and gn[0] > 0:
+        roofline["groupnorm_gbs"] = gn[3] / (gn[0] / 1000.0) / 1e9
+        roofline["groupnorm_frac_of_hbm"] = roofline["groupnorm_gbs"] / hbm
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, sample = cpu_oracle_forward_rate(wts, threads)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    launches = eng.forward_launches(B, H, W)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded inputs, seeded default-init weights)",
+            "config": config_dict(world), "clocks": clk, "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches * args.steps,
+            "tensor_peak_frac": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_burst,
+        }))
+    eng.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -48,6 +48,8 @@ typedef struct sdg_profile_row {
   char name[32];   /* op category: GN, LN, CONV3, GEMM, ATTN, GEMV, MISC */
   double ms;       /* summed device time of that category in one forward */
   int launches;
+  double flops;    /* algorithmic FLOPs of the category (2*M*N*K; attention 4*Sq*Sk*d per head) */
+  double bytes;    /* algorithmic HBM bytes (norms: 1 read + 1 write of the fp16 activation) */
 } sdg_profile_row;
 
 /* --- lifecycle --------------------------------------------------------------- */

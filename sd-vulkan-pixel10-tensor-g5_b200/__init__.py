@@ -46,7 +46,8 @@ class SdgError(RuntimeError):
 
 
 class ProfileRow(ctypes.Structure):
-    _fields_ = [("name", ctypes.c_char * 32), ("ms", ctypes.c_double), ("launches", ctypes.c_int)]
+    _fields_ = [("name", ctypes.c_char * 32), ("ms", ctypes.c_double), ("launches", ctypes.c_int),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
 _lib: Optional[ctypes.CDLL] = None
@@ -211,12 +212,13 @@ class Engine:
                                     out.ctypes.data))
         return out
 
-    def profile(self, B: int = 2, H: int = 64, W: int = 64) -> Dict[str, Tuple[float, int]]:
+    def profile(self, B: int = 2, H: int = 64, W: int = 64) -> Dict[str, Tuple[float, int, float, float]]:
+        """{category: (device ms, launches, algorithmic FLOPs, algorithmic bytes)} of one eager forward."""
         rows = (ProfileRow * 16)()
         n = lib().sdg_profile(self._h, B, H, W, rows, 16)
         if n < 0:
             raise SdgError(-n, last_error())
-        return {rows[i].name.decode(): (rows[i].ms, rows[i].launches) for i in range(n)}
+        return {rows[i].name.decode(): (rows[i].ms, rows[i].launches, rows[i].flops, rows[i].bytes) for i in range(n)}
 
     def forward_launches(self, B: int, H: int, W: int) -> int:
         return lib().sdg_forward_launches(self._h, B, H, W)

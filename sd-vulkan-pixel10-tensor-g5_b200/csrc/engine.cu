@@ -112,6 +112,7 @@ class Builder {
   // profiling: per-launch category events
   bool profile = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof;
+  double cat_flops[8] = {0}, cat_bytes[8] = {0};  // algorithmic work per category (counted in every mode)
 
  private:
   Engine& e_;
@@ -441,12 +442,14 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   a.gamma = n.g; a.beta = n.b; a.eps = eps; a.silu = silu ? 1 : 0; a.y = y;
   a.stats = dry_ ? nullptr : gn_stats_ + (size_t)gn_slot_ * gn_slot_floats_;
   gn_slot_++;
+  cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
   if (dry_ || !ok()) { launches_ += 2; return; }
   begin_op(kCatGN);
   check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 2);
 }
 
 void Builder::gemm(GemmArgs a, int cat) {
+  cat_flops[cat] += 2.0 * a.M * a.N * a.K;
   if (dry_ || !ok()) { launches_ += 1; return; }
   begin_op(cat);
   check(launch_gemm(a, pl_.dev_err, s_), cat == kCatConv3 ? "conv3x3" : "gemm", cat);
@@ -461,7 +464,7 @@ AttnBufs& Builder::level_bufs(int C, int S) {
   AttnBufs b;
   b.q = alloc_h(BH * S * dp);
   b.k = alloc_h(BH * S * dp);
-  b.vt = alloc_h(BH * d16 * S);
+  b.vt = alloc_h(BH * d16 * ((S + 7) / 8 * 8));
   return attn_[key] = b;
 }
 
@@ -524,6 +527,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
     gemm(a, kCatGemm);
   };
   auto ln = [&](const __half* xin, const Norm& n) {
+    cat_bytes[kCatLN] += 2.0 * 2.0 * M * C;
     if (dry_ || !ok()) { launches_++; return; }
     begin_op(kCatLN);
     check(launch_layernorm(xin, M, C, n.g, n.b, kLnEps, hn, s_), "layernorm", kCatLN);
@@ -539,6 +543,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
     gemm(a, kCatGemm);
   };
   auto attn = [&](const __half* q, const __half* k, const __half* vt, int Sk, int vt_ld) {
+    cat_flops[kCatAttn] += 4.0 * B * kHeads * (double)S * Sk * d;
     if (dry_ || !ok()) { launches_++; return; }
     AttnArgs a;
     a.q = q; a.k = k; a.v = vt; a.BH = B * kHeads; a.heads = kHeads; a.Sq = S; a.Sk = Sk; a.d = d; a.dp = dp;
@@ -548,8 +553,9 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   };
   lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
   ln(tt, t.ln1);
-  heads(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, S);            // Q, K, V^T
-  attn(ab.q, ab.k, ab.vt, S, S);                                   // self-attention
+  const int spad = (S + 7) / 8 * 8;                                // V^T rows are 16-byte multiples
+  heads(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, spad);         // Q, K, V^T
+  attn(ab.q, ab.k, ab.vt, S, spad);                                // self-attention
   lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
   ln(tt, t.ln2);
   heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
@@ -1078,6 +1084,8 @@ SDG_API int sdg_profile(sdg_engine* h, int B, int H, int W, sdg_profile_row* row
     snprintf(rows[n].name, sizeof rows[n].name, "%s", sdg::kCatName[c]);
     rows[n].ms = ms[c];
     rows[n].launches = cnt[c];
+    rows[n].flops = b.cat_flops[c];
+    rows[n].bytes = b.cat_bytes[c];
     ++n;
   }
   return n;
