@@ -196,7 +196,8 @@ def main():
     d_lat, d_t, d_ctx = lat.to(dev), t.to(dev), ctx.to(dev)
     d_out = torch.empty_like(d_lat)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream(device=dev)          # non-default stream: events and forwards share it
+    torch.cuda.set_stream(stream)
 
     def step():
         eng.forward_device(d_lat, d_t, d_ctx, d_out, stream.cuda_stream)

@@ -98,7 +98,7 @@ SDG_API int sdg_unet_forward_tproj(sdg_engine* e, const float* latent, const flo
                                    const float* context, int B, int H, int W, float* out, void* stream);
 
 /* Device-pointer variant: same layouts, all pointers on the engine's device;
- * asynchronous on `stream` (NULL = engine stream). */
+ * asynchronous on `stream` (NULL = the CUDA legacy default stream). */
 SDG_API int sdg_unet_forward_device(sdg_engine* e, const float* latent, const float* timesteps, int n_t,
                                     const float* context, int B, int H, int W, float* out, void* stream);
 
@@ -149,11 +149,15 @@ SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const
                        const uint16_t* residual, int act, uint16_t* y, int* err_word, void* stream);
 
 /* GroupNorm(groups) (+SiLU) over x (optionally channel-concat [x ; x2]),
- * [B,HW,C1+C2] -> y. stats_scratch: device fp32[B*(C1+C2)*2], any contents
- * (zeroed here). */
+ * [B,HW,C1+C2] -> y. stats_scratch: device memory of at least
+ * sdg_groupnorm_scratch_bytes(B, HW, C1+C2, groups) bytes, any contents.
+ * Deterministic: per-image results do not depend on the batch. */
 SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,
                           const float* gamma, const float* beta, float eps, int silu, uint16_t* y,
                           float* stats_scratch, void* stream);
+
+/* Bytes of device scratch sdg_groupnorm needs for this shape (0 on bad input). */
+SDG_API size_t sdg_groupnorm_scratch_bytes(int B, int HW, int C, int groups);
 
 SDG_API int sdg_layernorm(const uint16_t* x, int M, int C, const float* gamma, const float* beta, float eps,
                           uint16_t* y, void* stream);

@@ -72,6 +72,7 @@ _SIGS = {
     "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, _P]),
     "sdg_groupnorm": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P, _P]),
+    "sdg_groupnorm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "sdg_layernorm": (_I, [_P, _I, _I, _P, _P, _F, _P, _P]),
     "sdg_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "sdg_add": (_I, [_P, _P, ctypes.c_size_t, _P, _P]),
@@ -98,7 +99,7 @@ def lib() -> ctypes.CDLL:
 def header_symbols() -> List[str]:
     """Every entry point declared in ``include/sdg.h``."""
     txt = open(HEADER).read()
-    return re.findall(r"SDG_API\s+int\s+(sdg_\w+)\s*\(", txt)
+    return re.findall(r"SDG_API\s+\w+\s+(sdg_\w+)\s*\(", txt)
 
 
 def last_error() -> str:
@@ -272,7 +273,8 @@ def groupnorm(x, gamma, beta, eps: float, silu: bool, x2=None, groups: int = 32,
     if out is None:
         out = torch.empty((B, HW, C1 + C2), dtype=torch.float16, device=x.device)
     if stats is None:
-        stats = torch.empty((B * (C1 + C2) * 2,), dtype=torch.float32, device=x.device)
+        nbytes = lib().sdg_groupnorm_scratch_bytes(B, HW, C1 + C2, groups)
+        stats = torch.empty((nbytes // 4 + 1,), dtype=torch.float32, device=x.device)
     check(lib().sdg_groupnorm(_ptr(x), _ptr(x2), B, HW, C1, C2, groups, _ptr(gamma), _ptr(beta), eps, int(silu),
                               _ptr(out), _ptr(stats), _stream(stream)))
     return out

@@ -139,9 +139,6 @@ SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, 
   if (!x || !y || !gamma || !beta || !stats_scratch || (x2 == nullptr) != (C2 == 0))
     return sdg::op_fail(SDG_ERR_ARG, "groupnorm: bad arguments");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t nst = (size_t)B * (C1 + C2) * 2;
-  cudaError_t e = cudaMemsetAsync(stats_scratch, 0, nst * 4, s);
-  if (e != cudaSuccess) return cuda_status(e, "groupnorm");
   sdg::GroupNormArgs a;
   a.x0 = reinterpret_cast<const __half*>(x); a.x1 = reinterpret_cast<const __half*>(x2);
   a.C0 = C1; a.C1 = C2; a.B = B; a.HW = HW; a.groups = groups;
@@ -149,6 +146,11 @@ SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, 
   a.y = reinterpret_cast<__half*>(y);
   a.stats = stats_scratch;
   return cuda_status(sdg::launch_groupnorm(a, s), "groupnorm");
+}
+
+SDG_API size_t sdg_groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
+  if (B <= 0 || HW <= 0 || C <= 0 || groups <= 0) return 0;
+  return sdg::groupnorm_scratch_bytes(B, HW, C, groups);
 }
 
 SDG_API int sdg_layernorm(const uint16_t* x, int M, int C, const float* gamma, const float* beta, float eps, uint16_t* y,

@@ -123,8 +123,6 @@ class Builder {
   int launches_ = 0;
   int status_ = SDG_OK;
   int gn_slot_ = 0;
-  float* gn_stats_ = nullptr;
-  size_t gn_slot_floats_ = 0;
   std::map<long, AttnBufs> attn_;
   std::vector<CrossBufs> cross_;
   int cross_idx_ = 0;
@@ -440,12 +438,12 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   a.x1 = x2 ? x2->p : nullptr; a.C1 = x2 ? x2->C : 0;
   a.B = B; a.HW = HW; a.groups = 32;
   a.gamma = n.g; a.beta = n.b; a.eps = eps; a.silu = silu ? 1 : 0; a.y = y;
-  a.stats = dry_ ? nullptr : gn_stats_ + (size_t)gn_slot_ * gn_slot_floats_;
+  a.stats = static_cast<float*>(alloc(groupnorm_scratch_bytes(B, HW, a.C0 + a.C1, 32)));  // scope scratch
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
-  if (dry_ || !ok()) { launches_ += 2; return; }
+  if (dry_ || !ok()) { launches_ += 3; return; }
   begin_op(kCatGN);
-  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 2);
+  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 3);
 }
 
 void Builder::gemm(GemmArgs a, int cat) {
@@ -622,9 +620,6 @@ int Builder::run() {
   pl_.ctx_in = alloc_f((size_t)B * kCtxLen * kCtxDim);
   pl_.out = alloc_f((size_t)B * 4 * HW);
   pl_.dev_err = static_cast<int*>(alloc(256));
-  gn_slot_floats_ = (size_t)B * 2560 * 2;
-  const int kGnSlots = 64;
-  gn_stats_ = alloc_f(gn_slot_floats_ * kGnSlots);
   {
     int h = H, ww = W;
     for (int i = 0; i < 3; ++i) { level_bufs(kBlockOut[i], h * ww); h /= 2; ww /= 2; }
@@ -645,8 +640,6 @@ int Builder::run() {
   (void)persistent_end;
 
   if (!dry_) {
-    begin_op(kCatMisc);
-    check(cudaMemsetAsync(gn_stats_, 0, gn_slot_floats_ * kGnSlots * 4, s_), "memset", kCatMisc, 0);
     begin_op(kCatMisc);
     check(launch_time_embedding(pl_.t_in, B, B, pl_.mode == 1 ? pl_.tproj_in : nullptr, te, s_), "time_embedding", kCatMisc);
     begin_op(kCatGemv);
@@ -939,7 +932,7 @@ SDG_API int sdg_unet_forward_device(sdg_engine* h, const float* latent, const fl
   sdg::Plan* p = nullptr;
   int st = e.get_plan(B, H, W, 0, &p);
   if (st) return st;
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL = the legacy default stream
   const size_t L = (size_t)B * 4 * H * W;
   SDG_CUDA_TRY(cudaMemcpyAsync(p->lat_in, latent, L * 4, cudaMemcpyDeviceToDevice, s));
   for (int b = 0; b < B; ++b)

@@ -4,14 +4,17 @@
 // (vk_engine.cpp:548-549): statistics per (image, group), y = (x-mu)*rstd*g+b,
 // optional SiLU. The reference reduces one group per workgroup with
 // var = E[x^2] - mu^2 (groupnorm_f32.comp:24-25); here the work is split for
-// bandwidth instead:
-//   pass 1 (stats): blocks of (image, pixel chunk); each thread owns one
-//     128-bit vector of 8 channels and accumulates shifted sums
-//     S1 = sum(x-K_c), S2 = sum((x-K_c)^2) with K_c = x[img, pixel 0, c]
-//     (the shift removes the E[x^2]-mu^2 cancellation); per-channel partials
-//     are reduced in shared memory and added to a [B, C, 2] fp32 scratch.
-//   pass 2 (apply): each block folds the per-channel sums into per-group
-//     (mu, rstd) exactly, then streams its chunk with 128-bit loads/stores.
+// bandwidth and made exact and deterministic (no atomics):
+//   pass 1 (stats):   blocks of (pixel chunk, image); each thread owns one
+//                     128-bit vector of 8 channels; two passes over the chunk
+//                     (the second hits L1/L2) give per-channel chunk mean and
+//                     centred M2, reduced across thread rows in fixed order.
+//   pass 2 (combine): one block per (image, group) merges the chunk partials
+//                     with Chan's formula M2 = sum M2_i + n_i (mu_i - mu)^2
+//                     (all terms non-negative: no cancellation).
+//   pass 3 (apply):   128-bit loads/stores, per-channel scale/shift, SiLU.
+// The chunking depends only on (HW, C), never on the batch, so an image's
+// result does not depend on what else is in the batch.
 // The input may be a channel concat [x0 ; x1] (up-block skip connections),
 // read in place from both sources.
 #include <algorithm>
@@ -34,135 +37,159 @@ __device__ __forceinline__ const __half* gn_src(const GroupNormArgs& a, int c, s
   return a.x1 + pix * a.C1;
 }
 
-__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(GroupNormArgs a, int pix_per_block) {
-  const int C = a.C0 + a.C1;
-  const int nvec = C / 8;
-  const int img = blockIdx.y;
-  const int p_begin = blockIdx.x * pix_per_block;
-  const int p_end = min(a.HW, p_begin + pix_per_block);
-  __shared__ float s1[kGnMaxC];
-  __shared__ float s2[kGnMaxC];
-  for (int c = threadIdx.x; c < C; c += blockDim.x) { s1[c] = 0.f; s2[c] = 0.f; }
-  __syncthreads();
-  const size_t img_base = (size_t)img * a.HW;
-  // threads cover (vector, pixel-row) pairs; each thread keeps one channel vector fixed
-  const int rows = max(1, (int)blockDim.x / nvec);
-  const int vecs_per_pass = rows * nvec <= (int)blockDim.x ? nvec : (int)blockDim.x;
-  for (int v0 = 0; v0 < nvec; v0 += vecs_per_pass) {
-    const int t = threadIdx.x;
-    const int v = v0 + t % vecs_per_pass;
-    const int r = t / vecs_per_pass;
-    const int nrows = (vecs_per_pass == nvec) ? rows : 1;
-    if (v < nvec && r < nrows) {
-      const int c0 = v * 8;
-      int cl;
-      const __half* k_ptr = gn_src(a, c0, img_base, cl);
-      float K[8], S1[8], S2[8];
-      {
-        uint4 u = *reinterpret_cast<const uint4*>(k_ptr + cl);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __half22float2(h[e]);
-          K[2 * e] = f.x;
-          K[2 * e + 1] = f.y;
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) { S1[e] = 0.f; S2[e] = 0.f; }
-      for (int pix = p_begin + r; pix < p_end; pix += nrows) {
-        const __half* src = gn_src(a, c0, img_base + pix, cl);
-        uint4 u = *reinterpret_cast<const uint4*>(src + cl);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __half22float2(h[e]);
-          const float d0 = f.x - K[2 * e], d1 = f.y - K[2 * e + 1];
-          S1[2 * e] += d0; S2[2 * e] += d0 * d0;
-          S1[2 * e + 1] += d1; S2[2 * e + 1] += d1 * d1;
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        atomicAdd(&s1[c0 + e], S1[e]);
-        atomicAdd(&s2[c0 + e], S2[e]);
-      }
-    }
-  }
-  __syncthreads();
-  float* st = a.stats + (size_t)img * C * 2;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    atomicAdd(st + 2 * c, s1[c]);
-    atomicAdd(st + 2 * c + 1, s2[c]);
+  for (int e = 0; e < 4; ++e) {
+    float2 f = __half22float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
   }
 }
 
-__global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, int pix_per_block) {
+// partials layout: [B][nblk][C] float2 (chunk mean, chunk M2)
+__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(GroupNormArgs a, int ppb, float2* __restrict__ part) {
   const int C = a.C0 + a.C1;
-  const int G = a.groups;
-  const int cpg = C / G;
+  const int nvec = C / 8;
+  const int img = blockIdx.y;
+  const int nblk = gridDim.x;
+  const int p_begin = blockIdx.x * ppb;
+  const int p_end = min(a.HW, p_begin + ppb);
+  const float n = (float)(p_end - p_begin);
+  __shared__ float red[kGnMaxC];   // [rows][C] partial sums, then M2
+  __shared__ float mean_s[kGnMaxC];
+  const size_t img_base = (size_t)img * a.HW;
+  const int rows = nvec <= kGnThreads ? kGnThreads / nvec : 1;
+  const int per_pass = nvec <= kGnThreads ? nvec : kGnThreads;
+  const int r = threadIdx.x / per_pass;
+  for (int v0 = 0; v0 < nvec; v0 += per_pass) {
+    const int v = v0 + threadIdx.x % per_pass;
+    const bool active = r < rows && v < nvec;
+    const int c0 = v * 8;
+    float S[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) S[e] = 0.f;
+    if (active) {
+      for (int pix = p_begin + r; pix < p_end; pix += rows) {
+        int cl;
+        const __half* src = gn_src(a, c0, img_base + pix, cl);
+        float x[8];
+        load8(src + cl, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) S[e] += x[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red[r * (per_pass * 8) + (v - v0) * 8 + e] = S[e];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < per_pass * 8 && v0 * 8 + c < C; c += blockDim.x) {
+      float t = 0.f;
+      for (int rr = 0; rr < rows; ++rr) t += red[rr * (per_pass * 8) + c];
+      mean_s[v0 * 8 + c] = t / n;
+    }
+    __syncthreads();
+    float M[8], m[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { M[e] = 0.f; m[e] = active ? mean_s[c0 + e] : 0.f; }
+    if (active) {
+      for (int pix = p_begin + r; pix < p_end; pix += rows) {
+        int cl;
+        const __half* src = gn_src(a, c0, img_base + pix, cl);
+        float x[8];
+        load8(src + cl, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = x[e] - m[e];
+          M[e] += d * d;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red[r * (per_pass * 8) + (v - v0) * 8 + e] = M[e];
+    }
+    __syncthreads();
+    float2* dst = part + ((size_t)img * nblk + blockIdx.x) * C;
+    for (int c = threadIdx.x; c < per_pass * 8 && v0 * 8 + c < C; c += blockDim.x) {
+      float t = 0.f;
+      for (int rr = 0; rr < rows; ++rr) t += red[rr * (per_pass * 8) + c];
+      dst[v0 * 8 + c] = make_float2(mean_s[v0 * 8 + c], t);
+    }
+    __syncthreads();
+  }
+}
+
+// one block per (group, image): Chan merge of (chunk, channel) partials -> (mu, rstd)
+__global__ void __launch_bounds__(256) gn_combine_kernel(GroupNormArgs a, int ppb, int nblk,
+                                                         const float2* __restrict__ part, float2* __restrict__ gstat) {
+  const int C = a.C0 + a.C1;
+  const int g = blockIdx.x, img = blockIdx.y;
+  const int cpg = C / a.groups;
+  const int items = nblk * cpg;
+  __shared__ float red[256];
+  const float2* base = part + (size_t)img * nblk * C + g * cpg;
+  auto n_of = [&](int blk) { return (float)(min(a.HW, (blk + 1) * ppb) - blk * ppb); };
+  // mean = sum n_i mu_i / N
+  float s = 0.f;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int blk = i / cpg, j = i % cpg;
+    s += n_of(blk) * base[(size_t)blk * C + j].x;
+  }
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 128; o; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  const float N = (float)a.HW * cpg;
+  const float mu = red[0] / N;
+  __syncthreads();
+  float m2 = 0.f;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int blk = i / cpg, j = i % cpg;
+    const float2 pr = base[(size_t)blk * C + j];
+    const float d = pr.x - mu;
+    m2 += pr.y + n_of(blk) * d * d;
+  }
+  red[threadIdx.x] = m2;
+  __syncthreads();
+  for (int o = 128; o; o >>= 1) {
+    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) gstat[img * a.groups + g] = make_float2(mu, rsqrtf(red[0] / N + a.eps));
+}
+
+__global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, int ppb, const float2* __restrict__ gstat) {
+  const int C = a.C0 + a.C1;
+  const int cpg = C / a.groups;
   const int img = blockIdx.y;
   __shared__ float sc[kGnMaxC];
   __shared__ float sh[kGnMaxC];
-  __shared__ float gmu[64];
-  __shared__ float grs[64];
-  const float* st = a.stats + (size_t)img * C * 2;
-  const size_t img_base = (size_t)img * a.HW;
-  const float n = (float)a.HW;
-  const float Ng = (float)a.HW * cpg;
-  // per-group mean / rstd from per-channel shifted sums (one warp per group)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int g = warp; g < G; g += blockDim.x / 32) {
-    float sum = 0.f;
-    for (int j = lane; j < cpg; j += 32) {
-      const int c = g * cpg + j;
-      int cl;
-      const __half* kp = gn_src(a, c, img_base, cl);
-      const float K = __half2float(kp[cl]);
-      sum += K * n + st[2 * c];
-    }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mu = sum / Ng;
-    float m2 = 0.f;
-    for (int j = lane; j < cpg; j += 32) {
-      const int c = g * cpg + j;
-      int cl;
-      const __half* kp = gn_src(a, c, img_base, cl);
-      const float dK = __half2float(kp[cl]) - mu;
-      m2 += st[2 * c + 1] + 2.f * dK * st[2 * c] + n * dK * dK;
-    }
-    for (int o = 16; o; o >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
-    if (lane == 0) {
-      gmu[g] = mu;
-      grs[g] = rsqrtf(fmaxf(m2 / Ng, 0.f) + a.eps);
-    }
-  }
-  __syncthreads();
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    const int g = c / cpg;
-    const float s = grs[g] * a.gamma[c];
+    const float2 st = gstat[img * a.groups + c / cpg];
+    const float s = st.y * a.gamma[c];
     sc[c] = s;
-    sh[c] = a.beta[c] - gmu[g] * s;
+    sh[c] = a.beta[c] - st.x * s;
   }
   __syncthreads();
+  const size_t img_base = (size_t)img * a.HW;
   const int nvec = C / 8;
-  const int p_begin = blockIdx.x * pix_per_block;
-  const int p_end = min(a.HW, p_begin + pix_per_block);
+  const int p_begin = blockIdx.x * ppb;
+  const int p_end = min(a.HW, p_begin + ppb);
   const size_t total = (size_t)(p_end - p_begin) * nvec;
   for (size_t i = threadIdx.x; i < total; i += blockDim.x) {
     const int pix = p_begin + (int)(i / nvec);
     const int c0 = (int)(i % nvec) * 8;
     int cl;
     const __half* src = gn_src(a, c0, img_base + pix, cl);
-    uint4 u = *reinterpret_cast<const uint4*>(src + cl);
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    float x[8];
+    load8(src + cl, x);
     uint4 o;
     uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float2 f = __half22float2(h[e]);
-      float y0 = f.x * sc[c0 + 2 * e] + sh[c0 + 2 * e];
-      float y1 = f.y * sc[c0 + 2 * e + 1] + sh[c0 + 2 * e + 1];
+      float y0 = x[2 * e] * sc[c0 + 2 * e] + sh[c0 + 2 * e];
+      float y1 = x[2 * e + 1] * sc[c0 + 2 * e + 1] + sh[c0 + 2 * e + 1];
       if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
       ow[e] = pack_half2(y0, y1);
     }
@@ -235,22 +262,32 @@ __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, i
 
 }  // namespace
 
+// Pixels per GroupNorm chunk: ~16 KB of input per block (second stats pass
+// stays in L1). Depends only on (HW, C) so results are batch-invariant.
+static int gn_ppb(int HW, int C) { return std::max(1, std::min(HW, (16 * 1024) / (2 * C))); }
+
+size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
+  const int ppb = gn_ppb(HW, C);
+  const int nblk = (HW + ppb - 1) / ppb;
+  return (size_t)B * nblk * C * sizeof(float2) + (size_t)B * groups * sizeof(float2);
+}
+
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
   const int C = a.C0 + a.C1;
   if (C <= 0 || C > kGnMaxC || C % 8 || a.C0 % 8 || (a.C1 && a.x1 == nullptr) || a.groups <= 0 || a.groups > 64 ||
       C % a.groups || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
     return cudaErrorInvalidValue;
-  // pixel chunk: ~256 KB of input per block, at least 4 pixels, and enough
-  // blocks to cover every SM a few times
-  const int bytes_per_pix = C * 2;
-  int ppb = std::max(4, (256 * 1024) / bytes_per_pix);
-  const int want_blocks = num_sms() * 4;
-  while (ppb > 4 && (long)a.B * ((a.HW + ppb - 1) / ppb) < want_blocks) ppb /= 2;
-  dim3 grid((a.HW + ppb - 1) / ppb, a.B);
-  gn_stats_kernel<<<grid, kGnThreads, 0, s>>>(a, ppb);
+  const int ppb = gn_ppb(a.HW, C);
+  const int nblk = (a.HW + ppb - 1) / ppb;
+  float2* part = reinterpret_cast<float2*>(a.stats);
+  float2* gstat = part + (size_t)a.B * nblk * C;
+  gn_stats_kernel<<<dim3(nblk, a.B), kGnThreads, 0, s>>>(a, ppb, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gn_apply_kernel<<<grid, kGnThreads, 0, s>>>(a, ppb);
+  gn_combine_kernel<<<dim3(a.groups, a.B), 256, 0, s>>>(a, ppb, nblk, part, gstat);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gn_apply_kernel<<<dim3(nblk, a.B), kGnThreads, 0, s>>>(a, ppb, gstat);
   return cudaGetLastError();
 }
 

@@ -53,7 +53,7 @@ struct GemmArgs {
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
-// tensors. stats: scratch of B*(C0+C1)*2 floats, zeroed by the caller.
+// tensors. stats: scratch of groupnorm_scratch_bytes() bytes (any contents).
 struct GroupNormArgs {
   const __half* x0 = nullptr; const __half* x1 = nullptr;
   int C0 = 0, C1 = 0, B = 1, HW = 1, groups = 32;
@@ -63,6 +63,7 @@ struct GroupNormArgs {
   float* stats = nullptr;
 };
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s);
+size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups);
 
 cudaError_t launch_layernorm(const __half* x, int M, int C, const float* gamma, const float* beta, float eps,
                              __half* y, cudaStream_t s);
