@@ -170,4 +170,5 @@ def test_bad_shape_and_missing_weight_are_reported(sdg, cuda, engine):
 def test_profile_categories(engine):
     prof = engine.profile(2, 32, 32)
     assert {"GN", "CONV3", "GEMM", "ATTN"} <= set(prof)
-    assert all(ms > 0 for ms, _ in prof.values())
+    assert all(ms > 0 for ms, _, _, _ in prof.values())
+    assert prof["CONV3"][2] > 0 and prof["GN"][3] > 0          # algorithmic FLOPs / bytes accounted
