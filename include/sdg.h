@@ -159,6 +159,23 @@ SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, 
 /* Bytes of device scratch sdg_groupnorm needs for this shape (0 on bad input). */
 SDG_API size_t sdg_groupnorm_scratch_bytes(int B, int HW, int C, int groups);
 
+/* sdg_groupnorm without the stats_scratch argument: it allocates nothing.
+ * No counterpart in the reference (whose engine allocates its own buffers).
+ * For callers that cannot allocate device memory themselves — e.g. a JNI or
+ * other foreign-language front end that reaches this library only through
+ * the C ABI and has no CUDA runtime of its own. The scratch is a fixed array
+ * of sdg_groupnorm_noalloc_max_scratch_bytes() bytes (8 MiB) inside the
+ * library, held on every GPU that loads it until the process exits; shapes
+ * needing more (see sdg_groupnorm_scratch_bytes) return SDG_ERR_SHAPE.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture. All calls share the one array: calls
+ * that overlap on the GPU (different streams, or different host threads
+ * without ordering) race and must be serialised by the caller. */
+SDG_API int sdg_groupnorm_noalloc(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,
+                                  const float* gamma, const float* beta, float eps, int silu, uint16_t* y,
+                                  void* stream);
+SDG_API size_t sdg_groupnorm_noalloc_max_scratch_bytes(void);
+
 SDG_API int sdg_layernorm(const uint16_t* x, int M, int C, const float* gamma, const float* beta, float eps,
                           uint16_t* y, void* stream);
 

@@ -73,6 +73,8 @@ _SIGS = {
     "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, _P]),
     "sdg_groupnorm": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P, _P]),
     "sdg_groupnorm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I, _I]),
+    "sdg_groupnorm_noalloc": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P]),
+    "sdg_groupnorm_noalloc_max_scratch_bytes": (ctypes.c_size_t, []),
     "sdg_layernorm": (_I, [_P, _I, _I, _P, _P, _F, _P, _P]),
     "sdg_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "sdg_add": (_I, [_P, _P, ctypes.c_size_t, _P, _P]),
@@ -277,6 +279,19 @@ def groupnorm(x, gamma, beta, eps: float, silu: bool, x2=None, groups: int = 32,
         stats = torch.empty((nbytes // 4 + 1,), dtype=torch.float32, device=x.device)
     check(lib().sdg_groupnorm(_ptr(x), _ptr(x2), B, HW, C1, C2, groups, _ptr(gamma), _ptr(beta), eps, int(silu),
                               _ptr(out), _ptr(stats), _stream(stream)))
+    return out
+
+
+def groupnorm_noalloc(x, gamma, beta, eps: float, silu: bool, x2=None, groups: int = 32, out=None, stream=None):
+    """Same as :func:`groupnorm` but through the entry point that allocates
+    nothing (its scratch is a fixed array inside the library)."""
+    import torch
+    B, HW, C1 = x.shape
+    C2 = 0 if x2 is None else x2.shape[2]
+    if out is None:
+        out = torch.empty((B, HW, C1 + C2), dtype=torch.float16, device=x.device)
+    check(lib().sdg_groupnorm_noalloc(_ptr(x), _ptr(x2), B, HW, C1, C2, groups, _ptr(gamma), _ptr(beta), eps,
+                                      int(silu), _ptr(out), _stream(stream)))
     return out
 
 
