@@ -136,17 +136,21 @@ SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
 /* y = conv(x) (+bias[Co]) (+rowbias[b,Co]) (+residual) (act: 0 none, 1 SiLU).
  * x is [B,H,W,Ci1], x2 (optional, channel concat after x) [B,H,W,Ci2].
  * k = 3 (pad 1, stride 1 or 2) or 1. y is [B,Ho,Wo,Co]. For stride 2 the
- * caller supplies col_scratch of B*Ho*Wo*9*Ci fp16 (else NULL). */
+ * caller supplies col_scratch of B*Ho*Wo*9*Ci fp16 (else NULL).
+ * workspace (optional, fp32-aligned device memory): when the tile chooser
+ * splits K across CTAs (small M, large K) it needs up to 32*M*Co*4 bytes; with
+ * less (or NULL) the op runs without split-K. */
 SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int W, int Ci1, int Ci2,
                        const uint16_t* w, const float* bias, int Co, int k, int stride, const float* rowbias,
-                       const uint16_t* residual, int act, uint16_t* y, uint16_t* col_scratch, int* err_word,
-                       void* stream);
+                       const uint16_t* residual, int act, uint16_t* y, uint16_t* col_scratch, void* workspace,
+                       size_t workspace_bytes, int* err_word, void* stream);
 
 /* y[M,N] = x[M,K] * w[N,K]^T (+bias) (+residual) (act: 0 none, 1 SiLU,
  * 2 GEGLU: w rows arranged in 256-row tiles [128 value rows ; 128 gate rows],
  * y is [M, N/2]). */
 SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
-                       const uint16_t* residual, int act, uint16_t* y, int* err_word, void* stream);
+                       const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
+                       int* err_word, void* stream);
 
 /* GroupNorm(groups) (+SiLU) over x (optionally channel-concat [x ; x2]),
  * [B,HW,C1+C2] -> y. stats_scratch: device memory of at least
@@ -164,9 +168,10 @@ SDG_API size_t sdg_groupnorm_scratch_bytes(int B, int HW, int C, int groups);
  * For callers that cannot allocate device memory themselves — e.g. a JNI or
  * other foreign-language front end that reaches this library only through
  * the C ABI and has no CUDA runtime of its own. The scratch is a fixed array
- * of sdg_groupnorm_noalloc_max_scratch_bytes() bytes (8 MiB) inside the
- * library, held on every GPU that loads it until the process exits; shapes
- * needing more (see sdg_groupnorm_scratch_bytes) return SDG_ERR_SHAPE.
+ * of sdg_groupnorm_noalloc_max_scratch_bytes() bytes (64 KiB: batch * groups
+ * <= 8192) inside the library, held on every GPU that loads it until the
+ * process exits; shapes needing more (see sdg_groupnorm_scratch_bytes) return
+ * SDG_ERR_SHAPE.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture. All calls share the one array: calls
  * that overlap on the GPU (different streams, or different host threads

@@ -69,8 +69,9 @@ _SIGS = {
     "sdg_lcm_denoise": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P]),
     "sdg_profile": (_I, [_P, _I, _I, _I, ctypes.POINTER(ProfileRow), _I]),
     "sdg_forward_launches": (_I, [_P, _I, _I, _I]),
-    "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
-    "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, _P]),
+    "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, ctypes.c_size_t, _P,
+                        _P]),
+    "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
     "sdg_groupnorm": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P, _P]),
     "sdg_groupnorm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "sdg_groupnorm_noalloc": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P]),
@@ -240,7 +241,7 @@ class Engine:
 
 # ------------------------------------------------------------------ op surface (torch CUDA tensors)
 def conv2d(x, w, bias, Co: int, k: int = 3, stride: int = 1, x2=None, rowbias=None, residual=None, act: int = 0,
-           out=None, col_scratch=None, err_word=None, stream=None):
+           out=None, col_scratch=None, workspace=None, err_word=None, stream=None):
     """x [B,H,W,Ci1] fp16 (x2 [B,H,W,Ci2] concatenated after it), w [Co][k*k][Ci] fp16."""
     import torch
     B, H, W, Ci1 = x.shape
@@ -250,20 +251,23 @@ def conv2d(x, w, bias, Co: int, k: int = 3, stride: int = 1, x2=None, rowbias=No
         out = torch.empty((B, Ho, Wo, Co), dtype=torch.float16, device=x.device)
     if stride == 2 and col_scratch is None:
         col_scratch = torch.empty((B * Ho * Wo * 9 * (Ci1 + Ci2),), dtype=torch.float16, device=x.device)
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().sdg_conv2d(_ptr(x), _ptr(x2), B, H, W, Ci1, Ci2, _ptr(w), _ptr(bias), Co, k, stride, _ptr(rowbias),
-                           _ptr(residual), act, _ptr(out), _ptr(col_scratch), _ptr(err_word), _stream(stream)))
+                           _ptr(residual), act, _ptr(out), _ptr(col_scratch), _ptr(workspace), wsb, _ptr(err_word),
+                           _stream(stream)))
     return out
 
 
-def linear(x, w, bias=None, residual=None, act: int = 0, out=None, err_word=None, stream=None):
+def linear(x, w, bias=None, residual=None, act: int = 0, out=None, workspace=None, err_word=None, stream=None):
     """x [M,K] fp16, w [N,K] fp16 -> [M,N] (act 2 = GEGLU on 256-row [value;gate] tiles -> [M,N/2])."""
     import torch
     M, K = x.shape
     N = w.shape[0]
     if out is None:
         out = torch.empty((M, N // 2 if act == 2 else N), dtype=torch.float16, device=x.device)
-    check(lib().sdg_linear(_ptr(x), M, K, _ptr(w), _ptr(bias), N, _ptr(residual), act, _ptr(out), _ptr(err_word),
-                           _stream(stream)))
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().sdg_linear(_ptr(x), M, K, _ptr(w), _ptr(bias), N, _ptr(residual), act, _ptr(out), _ptr(workspace),
+                           wsb, _ptr(err_word), _stream(stream)))
     return out
 
 

@@ -73,7 +73,8 @@ extern "C" {
 
 SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int W, int Ci1, int Ci2, const uint16_t* w,
                        const float* bias, int Co, int k, int stride, const float* rowbias, const uint16_t* residual,
-                       int act, uint16_t* y, uint16_t* col_scratch, int* err_word, void* stream) {
+                       int act, uint16_t* y, uint16_t* col_scratch, void* workspace, size_t workspace_bytes,
+                       int* err_word, void* stream) {
   if (!x || !w || !y || B <= 0 || H <= 0 || W <= 0 || Ci1 <= 0 || Co <= 0 || (x2 == nullptr) != (Ci2 == 0))
     return sdg::op_fail(SDG_ERR_ARG, "conv2d: bad arguments");
   if (!(k == 1 || k == 3) || !(stride == 1 || stride == 2) || (k == 1 && stride != 1))
@@ -90,6 +91,8 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
   a.residual = reinterpret_cast<const __half*>(residual);
   a.act = act == 1 ? 1 : 0;
   a.out = reinterpret_cast<__half*>(y);
+  a.ws = static_cast<float*>(workspace);
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   if (k == 3 && stride == 2) {
     if (x2) return sdg::op_fail(SDG_ERR_SHAPE, "conv2d: stride 2 takes one source");
     if (!col_scratch) return sdg::op_fail(SDG_ERR_ARG, "conv2d: stride 2 needs col_scratch");
@@ -114,7 +117,8 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
 }
 
 SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
-                       const uint16_t* residual, int act, uint16_t* y, int* err_word, void* stream) {
+                       const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
+                       int* err_word, void* stream) {
   if (!x || !w || !y || M <= 0 || K <= 0 || N <= 0) return sdg::op_fail(SDG_ERR_ARG, "linear: bad arguments");
   sdg::GemmArgs a;
   a.M = M; a.N = N; a.K = K; a.taps = 1;
@@ -123,6 +127,8 @@ SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const
   a.bias = bias;
   a.residual = reinterpret_cast<const __half*>(residual);
   a.out = reinterpret_cast<__half*>(y);
+  a.ws = static_cast<float*>(workspace);
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   if (act == 2) {
     if (residual) return sdg::op_fail(SDG_ERR_ARG, "linear: GEGLU takes no residual");
     a.epi = sdg::kEpiGeglu;

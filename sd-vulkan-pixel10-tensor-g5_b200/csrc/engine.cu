@@ -441,16 +441,24 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   a.stats = static_cast<float*>(alloc(groupnorm_scratch_bytes(B, HW, a.C0 + a.C1, 32)));  // scope scratch
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
-  if (dry_ || !ok()) { launches_ += 3; return; }
+  if (dry_ || !ok()) { launches_ += 2; return; }
   begin_op(kCatGN);
-  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 3);
+  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 2);
 }
 
 void Builder::gemm(GemmArgs a, int cat) {
   cat_flops[cat] += 2.0 * a.M * a.N * a.K;
-  if (dry_ || !ok()) { launches_ += 1; return; }
+  const size_t mark = off_;  // split-K workspace lives only until the GEMM's reduce pass
+  a.ws_bytes = gemm_workspace_bytes(a);
+  a.ws = a.ws_bytes ? alloc_f(a.ws_bytes / 4) : nullptr;
+  if (dry_ || !ok()) {
+    launches_ += a.ws_bytes ? 2 : 1;
+    off_ = mark;
+    return;
+  }
   begin_op(cat);
-  check(launch_gemm(a, pl_.dev_err, s_), cat == kCatConv3 ? "conv3x3" : "gemm", cat);
+  check(launch_gemm(a, pl_.dev_err, s_), cat == kCatConv3 ? "conv3x3" : "gemm", cat, gemm_launch_count(a));
+  off_ = mark;
 }
 
 AttnBufs& Builder::level_bufs(int C, int S) {

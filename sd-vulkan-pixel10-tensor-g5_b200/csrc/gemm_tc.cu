@@ -9,7 +9,13 @@
 //               bias / residual / SiLU / GEGLU / head scatter, fp16 stores
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps
 // the main loop of tile i+1. No cluster multicast is used anywhere.
+//
+// Split-K: when M is small (deep UNet levels) the K range is divided among
+// CTAs; each writes fp32 partials to a workspace and a reduce kernel sums the
+// splits in a fixed order and applies the same fused epilogue, so results are
+// deterministic.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 
 #include "sdg_kernels.h"
@@ -28,7 +34,7 @@ constexpr uint32_t kATileBytes = BM * BK * 2;  // 16 KB
 struct GemmDev {
   int M, N, K;
   int taps, cin0, cin1;
-  int H, W, box_h, box_b;  // conv geometry
+  int H, W;                // conv geometry
   int epi, act;
   const float* bias;
   const float* rowbias;
@@ -44,6 +50,8 @@ struct GemmDev {
   __half* head_out2;
   int head_C, heads, head_d, head_dp;
   int head_vt, head_d16, head_spad;
+  int splits, kb_per_split;  // split-K
+  float* ws;                 // [splits][M][N] fp32 partials when splits > 1
   int* err;
 };
 
@@ -59,37 +67,76 @@ struct Cfg {
   static_assert(kSmem <= 232448, "GEMM tile configuration exceeds 227 KB of shared memory");
 };
 
-__device__ __forceinline__ void store_row_chunk(__half* dst, const float* v, int n) {
-  // n is 16 or 32 consecutive fp16 (16-byte aligned destination)
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ void load8h(const __half* src, float (&v)[8]) {
+  uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    if (q * 8 < n) {
-      uint4 u;
-      u.x = pack_half2(v[q * 8 + 0], v[q * 8 + 1]);
-      u.y = pack_half2(v[q * 8 + 2], v[q * 8 + 3]);
-      u.z = pack_half2(v[q * 8 + 4], v[q * 8 + 5]);
-      u.w = pack_half2(v[q * 8 + 6], v[q * 8 + 7]);
-      d4[q] = u;
-    }
+  for (int e = 0; e < 4; ++e) {
+    float2 f = __half22float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
   }
 }
 
-__device__ __forceinline__ void load_half_chunk(const __half* src, float* v, int n) {
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_half2(v[0], v[1]);
+  u.y = pack_half2(v[2], v[3]);
+  u.z = pack_half2(v[4], v[5]);
+  u.w = pack_half2(v[6], v[7]);
+  return u;
+}
+
+// Fused epilogue for 8 consecutive output columns [n, n+8) of row m (m < M).
+// Not used for GEGLU (which pairs two column ranges).
+__device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int n, float (&v)[8]) {
+  const int img = m / p.rows_per_image;
+  if (p.epi == kEpiNchwF32) {
+    const int pix = m - img * p.rows_per_image;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    if (q * 8 < n) {
-      uint4 u = __ldg(s4 + q);
-      const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __half22float2(h[e]);
-        v[q * 8 + 2 * e] = f.x;
-        v[q * 8 + 2 * e + 1] = f.y;
-      }
-    }
+    for (int j = 0; j < 8; ++j)
+      if (n + j < p.N)
+        p.out_f32[((size_t)img * p.N + n + j) * p.rows_per_image + pix] = v[j] + (p.bias ? __ldg(p.bias + n + j) : 0.f);
+    return;
   }
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += __ldg(p.bias + n + j);
+  }
+  if (p.rowbias) {
+    const float* rb = p.rowbias + (size_t)img * p.rowbias_ld + n;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += __ldg(rb + j);
+  }
+  if (p.residual) {
+    float rv[8];
+    load8h(p.residual + (size_t)m * p.ld_res + n, rv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += rv[j];
+  }
+  if (p.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+  }
+  if (p.epi == kEpiHeads) {
+    const int s_idx = m - img * p.rows_per_image;
+    const int which = n / p.head_C;
+    const int cc = n - which * p.head_C;
+    const int h = cc / p.head_d;
+    const int jj = cc - h * p.head_d;
+    __half* base = which == 0 ? p.head_out0 : (which == 1 ? p.head_out1 : p.head_out2);
+    if (which == p.head_vt) {
+      // transposed V: [BH, d16, spad]; consecutive rows of a warp are consecutive keys
+      __half* dst = base + (((size_t)img * p.heads + h) * p.head_d16 + jj) * p.head_spad + s_idx;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dst[(size_t)e * p.head_spad] = __float2half_rn(v[e]);
+      return;
+    }
+    __half* dst = base + (((size_t)img * p.heads + h) * p.rows_per_image + s_idx) * p.head_dp + jj;
+    *reinterpret_cast<uint4*>(dst) = pack8(v);
+    return;
+  }
+  *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + n) = pack8(v);
 }
 
 template <int BN>
@@ -117,9 +164,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  const int num_mn = num_m * num_n;
+  const int num_units = num_mn * p.splits;
   const int kb_per_tap = (p.cin0 + p.cin1) / BK;
   const int KB = p.K / BK;
+  // unit -> (m block, n block, k range); m fastest so co-resident CTAs share W tiles
+  auto decode = [&](int unit, int& m_blk, int& n_blk, int& kb0, int& kb1) {
+    const int ks = unit / num_mn;
+    const int r = unit - ks * num_mn;
+    m_blk = r % num_m;
+    n_blk = r / num_m;
+    kb0 = ks * p.kb_per_split;
+    kb1 = min(KB, kb0 + p.kb_per_split);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -155,8 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued[S];
       for (int s = 0; s < S; ++s) { issued[s] = false; last_phase[s] = 0; }
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % num_m, n_blk = tile / num_m;
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        int m_blk, n_blk, kb0, kb1;
+        decode(unit, m_blk, n_blk, kb0, kb1);
         const int m0 = m_blk * BM, n0 = n_blk * BN;
         int img0 = 0, y0 = 0;
         if (p.taps == 9) {
@@ -164,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           img0 = m0 / hw;
           y0 = (m0 % hw) / p.W;
         }
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
@@ -199,12 +257,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_f16(BM, BN, false);
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tl) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x, ++tl) {
+        int m_blk, n_blk, kb0, kb1;
+        decode(unit, m_blk, n_blk, kb0, kb1);
         const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
         if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
@@ -213,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t db = sdesc_sw128(smem_u32(sB + s * C::kBTileBytes), 16, 1024);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           mma_commit(empty_bar(s));
         }
         if (!ok) break;
@@ -228,16 +288,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lg = warp & 3;  // TMEM lane group this warp may access
     const int row = lg * 32 + lane;
     uint32_t tl = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tl) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++tl) {
+      int m_blk, n_blk, kb0, kb1;
+      decode(unit, m_blk, n_blk, kb0, kb1);
       const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int m_blk = tile % num_m, n_blk = tile / num_m;
       const int m = m_blk * BM + row;
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
-      const int img = mvalid ? m / p.rows_per_image : 0;
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
       constexpr int CH = C::kChunk;
       if (p.epi == kEpiGeglu) {
@@ -259,14 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           const int nc = nout0 + c;
           if (mvalid && nc < p.N / 2) {
-            float v[32];
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
-              const float a = __uint_as_float(ra[j]) + (p.bias ? __ldg(p.bias + n0 + c + j) : 0.f);
-              const float g = __uint_as_float(rg[j]) + (p.bias ? __ldg(p.bias + n0 + HALF + c + j) : 0.f);
-              v[j] = a * gelu_erf(g);
+            for (int g = 0; g < CH / 8; ++g) {
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int cj = c + g * 8 + j;
+                const float a = __uint_as_float(ra[g * 8 + j]) + (p.bias ? __ldg(p.bias + n0 + cj) : 0.f);
+                const float gt = __uint_as_float(rg[g * 8 + j]) + (p.bias ? __ldg(p.bias + n0 + HALF + cj) : 0.f);
+                v[j] = a * gelu_erf(gt);
+              }
+              *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc + g * 8) = pack8(v);
             }
-            store_row_chunk(p.out + (size_t)m * p.ld_out + nc, v, CH);
           }
         }
       } else {
@@ -284,63 +348,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
           const int n = n0 + c;
           if (!mvalid || n >= p.N) continue;
-          float v[32];
+          if (p.splits > 1) {
+            // raw fp32 partials; the reduce kernel applies the epilogue
+            const int ks = kb0 / p.kb_per_split;
+            float4* dst = reinterpret_cast<float4*>(p.ws + ((size_t)ks * p.M + m) * p.N + n);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) v[j] = __uint_as_float(r[j]);
-          if (p.epi == kEpiNchwF32) {
-            const int pix = m % p.rows_per_image;
-            for (int j = 0; j < CH && n + j < p.N; ++j) {
-              float x = v[j] + (p.bias ? __ldg(p.bias + n + j) : 0.f);
-              p.out_f32[((size_t)img * p.N + n + j) * p.rows_per_image + pix] = x;
-            }
+            for (int q = 0; q < CH / 4; ++q)
+              dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                                   __uint_as_float(r[4 * q + 3]));
             continue;
           }
-          if (p.bias) {
 #pragma unroll
-            for (int j = 0; j < CH; ++j) v[j] += __ldg(p.bias + n + j);
-          }
-          if (p.rowbias) {
-            const float* rb = p.rowbias + (size_t)img * p.rowbias_ld + n;
+          for (int g = 0; g < CH / 8; ++g) {
+            if (n + g * 8 >= p.N) break;
+            float v[8];
 #pragma unroll
-            for (int j = 0; j < CH; ++j) v[j] += __ldg(rb + j);
-          }
-          if (p.residual) {
-            float rv[32];
-            load_half_chunk(p.residual + (size_t)m * p.ld_res + n, rv, CH);
-#pragma unroll
-            for (int j = 0; j < CH; ++j) v[j] += rv[j];
-          }
-          if (p.act == 1) {
-#pragma unroll
-            for (int j = 0; j < CH; ++j) v[j] = silu_f(v[j]);
-          }
-          if (p.epi == kEpiHeads) {
-            const int s_idx = m % p.rows_per_image;
-#pragma unroll
-            for (int g = 0; g < CH / 8; ++g) {
-              const int nn = n + g * 8;
-              const int which = nn / p.head_C;
-              const int cc = nn - which * p.head_C;
-              const int h = cc / p.head_d;
-              const int jj = cc - h * p.head_d;
-              __half* base = which == 0 ? p.head_out0 : (which == 1 ? p.head_out1 : p.head_out2);
-              if (which == p.head_vt) {
-                // transposed V: [BH, d16, spad]; consecutive rows of the warp are consecutive keys
-                __half* dst = base + (((size_t)img * p.heads + h) * p.head_d16 + jj) * p.head_spad + s_idx;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) dst[(size_t)e * p.head_spad] = __float2half_rn(v[g * 8 + e]);
-                continue;
-              }
-              __half* dst = base + (((size_t)img * p.heads + h) * p.rows_per_image + s_idx) * p.head_dp + jj;
-              uint4 u;
-              u.x = pack_half2(v[g * 8 + 0], v[g * 8 + 1]);
-              u.y = pack_half2(v[g * 8 + 2], v[g * 8 + 3]);
-              u.z = pack_half2(v[g * 8 + 4], v[g * 8 + 5]);
-              u.w = pack_half2(v[g * 8 + 6], v[g * 8 + 7]);
-              *reinterpret_cast<uint4*>(dst) = u;
-            }
-          } else {
-            store_row_chunk(p.out + (size_t)m * p.ld_out + n, v, CH);
+            for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+            epilogue8(p, m, n + g * 8, v);
           }
         }
       }
@@ -358,9 +382,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Sum split-K partials in split order and apply the fused epilogue; one
+// thread per 8 output columns.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
+  const int ngrp = (p.N + 7) / 8;
+  const size_t total = (size_t)p.M * ngrp;
+  const size_t plane = (size_t)p.M * p.N;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / ngrp);
+    const int n = (int)(i % ngrp) * 8;
+    const float* src = p.ws + (size_t)m * p.N + n;
+    float v[8];
+    {
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(src + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    for (int s = 1; s < p.splits; ++s) {
+      const float4 a = *reinterpret_cast<const float4*>(src + s * plane);
+      const float4 b = *reinterpret_cast<const float4*>(src + s * plane + 4);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    epilogue8(p, m, n, v);
+  }
+}
+
 template <int BN>
-cudaError_t launch_bn(const GemmArgs& a, const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1,
-                      const CUtensorMap& mw, cudaStream_t s) {
+cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1, const CUtensorMap& mw,
+                      cudaStream_t s) {
   using C = Cfg<BN>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -370,27 +419,82 @@ cudaError_t launch_bn(const GemmArgs& a, const GemmDev& d, const CUtensorMap& ma
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-  const int grid = std::max(1, std::min(tiles, num_sms()));
+  const int units = ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.splits;
+  const int grid = std::max(1, std::min(units, num_sms()));
   gemm_tc_kernel<BN><<<grid, kThreads, C::kSmem, s>>>(ma0, ma1, mw, d);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || d.splits == 1) return e;
+  const size_t total = (size_t)d.M * ((d.N + 7) / 8);
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
+  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(d);
   return cudaGetLastError();
 }
 
-int choose_bn(const GemmArgs& a) {
-  if (a.bn) return a.bn;
-  if (a.N <= 16) return 16;
-  if (a.epi == kEpiGeglu) return 256;
-  // prefer the widest tile that divides N and still gives >= ~1 wave of tiles
+struct TileChoice {
+  int bn = 64, splits = 1, kb_per_split = 1;
+};
+
+// Cost model (cycles of the slowest CTA): per 64-deep k-block a CTA needs
+// max(MMA cycles, operand bytes / ~64 B per cycle of L2 bandwidth); waves of
+// units over the SMs; plus the split-K reduce traffic.
+TileChoice choose_tiles(const GemmArgs& a) {
+  TileChoice best;
+  const int KB = a.K / BK;
+  const int sms = num_sms();
   const int num_m = (a.M + BM - 1) / BM;
-  const int cands[4] = {256, 160, 128, 64};
-  for (int bn : cands) {
-    if (a.N % bn) continue;
-    if (num_m * (a.N / bn) >= num_sms() * 3 / 4 || bn == 64) return bn;
+  best.kb_per_split = KB;
+  if (a.bn) {
+    best.bn = a.bn;
+    return best;
   }
-  return a.N % 64 == 0 ? 64 : 128;
+  if (a.N <= 16) {
+    best.bn = 16;
+    return best;
+  }
+  if (a.epi == kEpiGeglu) {
+    best.bn = 256;
+    return best;
+  }
+  const int cands[4] = {256, 160, 128, 64};
+  double best_t = 1e30;
+  for (int bn : cands) {
+    if (a.N % bn != 0) continue;
+    const int tiles = num_m * (a.N / bn);
+    const double kcost = std::max(2.0 * bn, (kATileBytes + bn * BK * 2.0) / 64.0);
+    const int max_split = (a.epi == kEpiNchwF32) ? 1 : std::max(1, std::min(32, KB / 6));
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const int kbs = (KB + sp - 1) / sp;
+      const int real_sp = (KB + kbs - 1) / kbs;
+      if (real_sp != sp) continue;
+      const int units = tiles * sp;
+      const int waves = (units + sms - 1) / sms;
+      double t = (double)waves * (kbs * kcost + 600.0);  // + per-unit pipeline fill / epilogue
+      if (sp > 1) t += ((double)sp * a.M * a.N * 4.0 + a.M * a.N * 2.0) / 2500.0 + 3000.0;  // reduce pass
+      if (t < best_t * 0.97) {
+        best_t = t;
+        best.bn = bn;
+        best.splits = sp;
+        best.kb_per_split = kbs;
+      }
+    }
+  }
+  if (best_t == 1e30) best.bn = 64;  // N not a multiple of any tile: ragged 64-wide tiles
+  return best;
 }
 
 }  // namespace
+
+size_t gemm_workspace_bytes(const GemmArgs& a) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK) return 0;
+  const TileChoice t = choose_tiles(a);
+  return t.splits > 1 ? (size_t)t.splits * a.M * a.N * sizeof(float) : 0;
+}
+
+int gemm_launch_count(const GemmArgs& a) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK) return 1;
+  const TileChoice t = choose_tiles(a);
+  return (t.splits > 1 && a.ws != nullptr && a.ws_bytes >= (size_t)t.splits * a.M * a.N * sizeof(float)) ? 2 : 1;
+}
 
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   const int cin = a.cin0 + a.cin1;
@@ -399,12 +503,17 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
       (a.cin1 > 0 && a.a1 == nullptr))
     return cudaErrorInvalidValue;
   if (a.epi != kEpiNchwF32 && a.epi != kEpiGeglu && a.N % 16 != 0) return cudaErrorInvalidValue;
-  const int bn = choose_bn(a);
+  if ((a.epi == kEpiPlain || a.epi == kEpiHeads) && a.N > 16 && a.N % 32 != 0) return cudaErrorInvalidValue;
+  TileChoice tc = choose_tiles(a);
+  if (tc.splits > 1 && (a.ws == nullptr || a.ws_bytes < (size_t)tc.splits * a.M * a.N * sizeof(float))) {
+    tc.splits = 1;  // no workspace: single pass
+    tc.kb_per_split = a.K / BK;
+  }
+  const int bn = tc.bn;
   if (a.epi == kEpiGeglu && (a.N % bn != 0)) return cudaErrorInvalidValue;
   if (a.epi == kEpiHeads && (a.head_d % 8 != 0 || a.head_C % 8 != 0 || a.head_dp < a.head_d ||
                              (a.head_vt >= 0 && (a.head_d16 < a.head_d || a.head_spad < a.rows_per_image))))
     return cudaErrorInvalidValue;
-  if ((a.epi == kEpiPlain || a.epi == kEpiHeads) && a.N > 16 && a.N % 32 != 0) return cudaErrorInvalidValue;
 
   GemmDev d{};
   d.M = a.M; d.N = a.N; d.K = a.K;
@@ -419,23 +528,25 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.head_out0 = a.head_out[0]; d.head_out1 = a.head_out[1]; d.head_out2 = a.head_out[2];
   d.head_C = a.head_C; d.heads = a.heads; d.head_d = a.head_d; d.head_dp = a.head_dp;
   d.head_vt = a.head_vt; d.head_d16 = a.head_d16; d.head_spad = a.head_spad;
+  d.splits = tc.splits; d.kb_per_split = tc.kb_per_split; d.ws = a.ws;
   d.err = dev_err;
 
   CUtensorMap ma0{}, ma1{}, mw{};
   if (a.taps == 9) {
     const int hw = a.H * a.W;
+    int box_h, box_b;
     if (a.W > 128 || (BM % a.W) != 0) return cudaErrorInvalidValue;
     if (hw >= BM) {
-      d.box_h = BM / a.W; d.box_b = 1;
-      if (a.H % d.box_h) return cudaErrorInvalidValue;
+      box_h = BM / a.W; box_b = 1;
+      if (a.H % box_h) return cudaErrorInvalidValue;
     } else {
       if (BM % hw) return cudaErrorInvalidValue;
-      d.box_h = a.H; d.box_b = BM / hw;
+      box_h = a.H; box_b = BM / hw;
     }
     auto mk4 = [&](CUtensorMap* m, const __half* base, int c) {
       uint64_t dims[4] = {(uint64_t)c, (uint64_t)a.W, (uint64_t)a.H, (uint64_t)a.B};
       uint64_t str[3] = {(uint64_t)c * 2, (uint64_t)a.W * c * 2, (uint64_t)hw * c * 2};
-      uint32_t box[4] = {BK, (uint32_t)a.W, (uint32_t)d.box_h, (uint32_t)d.box_b};
+      uint32_t box[4] = {BK, (uint32_t)a.W, (uint32_t)box_h, (uint32_t)box_b};
       return make_tmap(m, base, 4, dims, str, box);
     };
     if (a.M != a.B * hw) return cudaErrorInvalidValue;
@@ -453,11 +564,11 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   if (!make_tmap_2d(&mw, a.w, a.N, a.K, a.K, bn, BK)) return cudaErrorInvalidValue;
 
   switch (bn) {
-    case 16: return launch_bn<16>(a, d, ma0, ma1, mw, s);
-    case 64: return launch_bn<64>(a, d, ma0, ma1, mw, s);
-    case 128: return launch_bn<128>(a, d, ma0, ma1, mw, s);
-    case 160: return launch_bn<160>(a, d, ma0, ma1, mw, s);
-    case 256: return launch_bn<256>(a, d, ma0, ma1, mw, s);
+    case 16: return launch_bn<16>(d, ma0, ma1, mw, s);
+    case 64: return launch_bn<64>(d, ma0, ma1, mw, s);
+    case 128: return launch_bn<128>(d, ma0, ma1, mw, s);
+    case 160: return launch_bn<160>(d, ma0, ma1, mw, s);
+    case 256: return launch_bn<256>(d, ma0, ma1, mw, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -3,20 +3,16 @@
 // GroupNorm replaces groupnorm_f32.comp / groupnorm_silu.comp
 // (vk_engine.cpp:548-549): statistics per (image, group), y = (x-mu)*rstd*g+b,
 // optional SiLU. The reference reduces one group per workgroup with
-// var = E[x^2] - mu^2 (groupnorm_f32.comp:24-25); here the work is split for
-// bandwidth and made exact and deterministic (no atomics):
-//   pass 1 (stats):   blocks of (pixel chunk, image); each thread owns one
-//                     128-bit vector of 8 channels; two passes over the chunk
-//                     (the second hits L1/L2) give per-channel chunk mean and
-//                     centred M2, reduced across thread rows in fixed order.
-//   pass 2 (combine): one block per (image, group) merges the chunk partials
-//                     with Chan's formula M2 = sum M2_i + n_i (mu_i - mu)^2
-//                     (all terms non-negative: no cancellation).
-//   pass 3 (apply):   128-bit loads/stores, per-channel scale/shift, SiLU.
-// The chunking depends only on (HW, C), never on the batch, so an image's
-// result does not depend on what else is in the batch.
+// var = E[x^2] - mu^2 (groupnorm_f32.comp:24-25). Here:
+//   kernel 1 (stats): one block per (group, image), exact two-pass mean and
+//                     centred variance over the group's elements read
+//                     straight from L2 (the producer just wrote them), fixed
+//                     reduction order -> deterministic, no atomics;
+//   kernel 2 (apply): 128-bit loads/stores over pixel chunks, per-channel
+//                     scale/shift from the group stats, optional SiLU.
 // The input may be a channel concat [x0 ; x1] (up-block skip connections),
-// read in place from both sources.
+// read in place from both sources. An image's result never depends on the
+// rest of the batch.
 #include <algorithm>
 
 #include "sdg_kernels.h"
@@ -26,6 +22,7 @@ namespace sdg {
 namespace {
 
 constexpr int kGnThreads = 256;
+constexpr int kGnStatThreads = 512;
 constexpr int kGnMaxC = 2560;
 
 __device__ __forceinline__ const __half* gn_src(const GroupNormArgs& a, int c, size_t pix, int& cl) {
@@ -48,115 +45,53 @@ __device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
   }
 }
 
-// partials layout: [B][nblk][C] float2 (chunk mean, chunk M2)
-__global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(GroupNormArgs a, int ppb, float2* __restrict__ part) {
-  const int C = a.C0 + a.C1;
-  const int nvec = C / 8;
-  const int img = blockIdx.y;
-  const int nblk = gridDim.x;
-  const int p_begin = blockIdx.x * ppb;
-  const int p_end = min(a.HW, p_begin + ppb);
-  const float n = (float)(p_end - p_begin);
-  __shared__ float red[kGnMaxC];   // [rows][C] partial sums, then M2
-  __shared__ float mean_s[kGnMaxC];
-  const size_t img_base = (size_t)img * a.HW;
-  const int rows = nvec <= kGnThreads ? kGnThreads / nvec : 1;
-  const int per_pass = nvec <= kGnThreads ? nvec : kGnThreads;
-  const int r = threadIdx.x / per_pass;
-  for (int v0 = 0; v0 < nvec; v0 += per_pass) {
-    const int v = v0 + threadIdx.x % per_pass;
-    const bool active = r < rows && v < nvec;
-    const int c0 = v * 8;
-    float S[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) S[e] = 0.f;
-    if (active) {
-      for (int pix = p_begin + r; pix < p_end; pix += rows) {
-        int cl;
-        const __half* src = gn_src(a, c0, img_base + pix, cl);
-        float x[8];
-        load8(src + cl, x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) S[e] += x[e];
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) red[r * (per_pass * 8) + (v - v0) * 8 + e] = S[e];
-    }
-    __syncthreads();
-    for (int c = threadIdx.x; c < per_pass * 8 && v0 * 8 + c < C; c += blockDim.x) {
-      float t = 0.f;
-      for (int rr = 0; rr < rows; ++rr) t += red[rr * (per_pass * 8) + c];
-      mean_s[v0 * 8 + c] = t / n;
-    }
-    __syncthreads();
-    float M[8], m[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) { M[e] = 0.f; m[e] = active ? mean_s[c0 + e] : 0.f; }
-    if (active) {
-      for (int pix = p_begin + r; pix < p_end; pix += rows) {
-        int cl;
-        const __half* src = gn_src(a, c0, img_base + pix, cl);
-        float x[8];
-        load8(src + cl, x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = x[e] - m[e];
-          M[e] += d * d;
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) red[r * (per_pass * 8) + (v - v0) * 8 + e] = M[e];
-    }
-    __syncthreads();
-    float2* dst = part + ((size_t)img * nblk + blockIdx.x) * C;
-    for (int c = threadIdx.x; c < per_pass * 8 && v0 * 8 + c < C; c += blockDim.x) {
-      float t = 0.f;
-      for (int rr = 0; rr < rows; ++rr) t += red[rr * (per_pass * 8) + c];
-      dst[v0 * 8 + c] = make_float2(mean_s[v0 * 8 + c], t);
-    }
-    __syncthreads();
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[32] = t;
   }
+  __syncthreads();
+  t = red[32];
+  __syncthreads();
+  return t;
 }
 
-// one block per (group, image): Chan merge of (chunk, channel) partials -> (mu, rstd)
-__global__ void __launch_bounds__(256) gn_combine_kernel(GroupNormArgs a, int ppb, int nblk,
-                                                         const float2* __restrict__ part, float2* __restrict__ gstat) {
+// one block per (group, image): exact mean / centred variance -> (mu, rstd)
+__global__ void __launch_bounds__(kGnStatThreads) gn_stats_kernel(GroupNormArgs a, float2* __restrict__ gstat) {
+  __shared__ float red[40];
   const int C = a.C0 + a.C1;
   const int g = blockIdx.x, img = blockIdx.y;
   const int cpg = C / a.groups;
-  const int items = nblk * cpg;
-  __shared__ float red[256];
-  const float2* base = part + (size_t)img * nblk * C + g * cpg;
-  auto n_of = [&](int blk) { return (float)(min(a.HW, (blk + 1) * ppb) - blk * ppb); };
-  // mean = sum n_i mu_i / N
+  const int pairs = cpg / 2;  // half2 per pixel of this group (C0 and cpg are even)
+  const int n_items = a.HW * pairs;
+  const size_t img_base = (size_t)img * a.HW;
+  auto item = [&](int i) -> float2 {
+    const int pix = i / pairs, j = i - (i / pairs) * pairs;
+    int cl;
+    const __half* src = gn_src(a, g * cpg + 2 * j, img_base + pix, cl);
+    return __half22float2(*reinterpret_cast<const __half2*>(src + cl));
+  };
   float s = 0.f;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    const int blk = i / cpg, j = i % cpg;
-    s += n_of(blk) * base[(size_t)blk * C + j].x;
-  }
-  red[threadIdx.x] = s;
-  __syncthreads();
-  for (int o = 128; o; o >>= 1) {
-    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-    __syncthreads();
+  for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
+    const float2 f = item(i);
+    s += f.x + f.y;
   }
   const float N = (float)a.HW * cpg;
-  const float mu = red[0] / N;
-  __syncthreads();
+  const float mu = block_sum(s, red) / N;
   float m2 = 0.f;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    const int blk = i / cpg, j = i % cpg;
-    const float2 pr = base[(size_t)blk * C + j];
-    const float d = pr.x - mu;
-    m2 += pr.y + n_of(blk) * d * d;
+  for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
+    const float2 f = item(i);
+    const float d0 = f.x - mu, d1 = f.y - mu;
+    m2 += d0 * d0 + d1 * d1;
   }
-  red[threadIdx.x] = m2;
-  __syncthreads();
-  for (int o = 128; o; o >>= 1) {
-    if (threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) gstat[img * a.groups + g] = make_float2(mu, rsqrtf(red[0] / N + a.eps));
+  const float var = block_sum(m2, red) / N;
+  if (threadIdx.x == 0) gstat[img * a.groups + g] = make_float2(mu, rsqrtf(var + a.eps));
 }
 
 __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, int ppb, const float2* __restrict__ gstat) {
@@ -262,31 +197,26 @@ __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, i
 
 }  // namespace
 
-// Pixels per GroupNorm chunk: ~16 KB of input per block (second stats pass
-// stays in L1). Depends only on (HW, C) so results are batch-invariant.
-static int gn_ppb(int HW, int C) { return std::max(1, std::min(HW, (16 * 1024) / (2 * C))); }
+// Pixels per apply block: ~32 KB of input, depends only on (HW, C).
+static int gn_ppb(int HW, int C) { return std::max(1, std::min(HW, (32 * 1024) / (2 * C))); }
 
 size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
-  const int ppb = gn_ppb(HW, C);
-  const int nblk = (HW + ppb - 1) / ppb;
-  return (size_t)B * nblk * C * sizeof(float2) + (size_t)B * groups * sizeof(float2);
+  (void)HW;
+  (void)C;
+  return (size_t)B * groups * sizeof(float2);
 }
 
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
   const int C = a.C0 + a.C1;
   if (C <= 0 || C > kGnMaxC || C % 8 || a.C0 % 8 || (a.C1 && a.x1 == nullptr) || a.groups <= 0 || a.groups > 64 ||
-      C % a.groups || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
+      C % a.groups || (C / a.groups) % 2 || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
     return cudaErrorInvalidValue;
-  const int ppb = gn_ppb(a.HW, C);
-  const int nblk = (a.HW + ppb - 1) / ppb;
-  float2* part = reinterpret_cast<float2*>(a.stats);
-  float2* gstat = part + (size_t)a.B * nblk * C;
-  gn_stats_kernel<<<dim3(nblk, a.B), kGnThreads, 0, s>>>(a, ppb, part);
+  float2* gstat = reinterpret_cast<float2*>(a.stats);
+  gn_stats_kernel<<<dim3(a.groups, a.B), kGnStatThreads, 0, s>>>(a, gstat);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  gn_combine_kernel<<<dim3(a.groups, a.B), 256, 0, s>>>(a, ppb, nblk, part, gstat);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  const int ppb = gn_ppb(a.HW, C);
+  const int nblk = (a.HW + ppb - 1) / ppb;
   gn_apply_kernel<<<dim3(nblk, a.B), kGnThreads, 0, s>>>(a, ppb, gstat);
   return cudaGetLastError();
 }

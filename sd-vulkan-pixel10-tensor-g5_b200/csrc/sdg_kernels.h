@@ -48,9 +48,15 @@ struct GemmArgs {
   int head_vt = -1;                 // index of the output stored transposed [BH, d16, head_spad]
   int head_d16 = 0, head_spad = 0;
   int bn = 0;                       // tile N (0 = choose)
+  float* ws = nullptr;              // split-K workspace (fp32); split-K only when large enough
+  size_t ws_bytes = 0;
 };
 
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s);
+// Workspace the tile chooser wants for split-K (0 = single pass).
+size_t gemm_workspace_bytes(const GemmArgs& a);
+// Kernel launches launch_gemm issues for these arguments (1, or 2 with split-K).
+int gemm_launch_count(const GemmArgs& a);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
 // tensors. stats: scratch of groupnorm_scratch_bytes() bytes (any contents).

@@ -36,8 +36,9 @@ def test_null_engine_is_rejected(sdg):
 
 def test_bad_op_arguments_are_rejected_without_gpu(sdg):
     L = sdg.lib()
-    assert L.sdg_linear(None, 1, 1, None, None, 1, None, 0, None, None, None) == 2   # SDG_ERR_ARG
-    assert L.sdg_conv2d(None, None, 1, 8, 8, 64, 0, None, None, 64, 5, 1, None, None, 0, None, None, None, None) == 2
+    assert L.sdg_linear(None, 1, 1, None, None, 1, None, 0, None, None, 0, None, None) == 2   # SDG_ERR_ARG
+    assert L.sdg_conv2d(None, None, 1, 8, 8, 64, 0, None, None, 64, 5, 1, None, None, 0, None, None, None, 0, None,
+                        None) == 2
 
 
 def test_init_without_device_fails_cleanly(sdg):

@@ -212,3 +212,33 @@ def test_upsample_concat_add(sdg, cuda, gen):
     s = sdg.add(a, a)
     torch.cuda.synchronize()
     assert torch.equal(s, a + a)
+
+
+# ---------------------------------------------------------------- split-K (deep levels: small M, large K)
+@pytest.mark.parametrize("M,N,K,resid", [(128, 1280, 11520, True), (512, 1280, 5120, False), (154, 640, 768, True),
+                                         (300, 320, 2880, False)])
+def test_linear_splitk(sdg, cuda, gen, M, N, K, resid):
+    x = rnd(M, K, g=gen).half()
+    w = rnd(N, K, std=1 / math.sqrt(K), g=gen).half()
+    b = rnd(N, std=0.1, g=gen).float()
+    r = rnd(M, N, g=gen).half() if resid else None
+    ws = torch.empty(32 * M * N, dtype=torch.float32, device=cuda)
+    y = sdg.linear(x, w, b, residual=r, workspace=ws)
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().T + b + (r.float() if resid else 0)
+    assert rel(y, ref) < TOL
+
+
+@pytest.mark.parametrize("B,C,H", [(2, 1280, 8), (2, 1280, 16), (2, 640, 32), (1, 2560, 8)])
+def test_conv3x3_splitk_rowbias_residual(sdg, cuda, gen, B, C, H):
+    Co = 1280 if C == 2560 else C
+    x = rnd(B, C, H, H, g=gen).half()
+    w = rnd(Co, C, 3, 3, std=1 / math.sqrt(9 * C), g=gen).half()
+    b = rnd(Co, std=0.1, g=gen).float()
+    rb = rnd(B, Co, std=0.5, g=gen).float()
+    res = rnd(B, Co, H, H, g=gen).half()
+    ws = torch.empty(32 * B * H * H * Co, dtype=torch.float32, device=cuda)
+    y = sdg.conv2d(nhwc(x), sdg.pack_conv_weight(w), b, Co, k=3, rowbias=rb, residual=nhwc(res), workspace=ws)
+    torch.cuda.synchronize()
+    ref = F.conv2d(x.float(), w.float(), b, padding=1) + rb[:, :, None, None] + res.float()
+    assert rel(nchw(y), ref) < TOL

@@ -52,8 +52,8 @@ def test_noalloc_groupnorm_matches_allocating_entry(sdg, cuda, B, C1, C2, H, sil
 
 def test_noalloc_groupnorm_rejects_oversized_shapes(sdg, cuda):
     cap = sdg.lib().sdg_groupnorm_noalloc_max_scratch_bytes()
-    assert cap == 8 << 20
-    B, H, C = 16, 64, 960
+    assert cap == 64 << 10
+    B, H, C = 300, 2, 64                     # 300 images x 32 groups needs 75 KiB of (mean, rstd) pairs
     assert sdg.lib().sdg_groupnorm_scratch_bytes(B, H * H, C, 32) > cap
     x = torch.zeros((B, H * H, C), dtype=torch.float16, device=cuda)
     g = torch.ones(C, device=cuda)
