@@ -441,9 +441,9 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   a.stats = static_cast<float*>(alloc(groupnorm_scratch_bytes(B, HW, a.C0 + a.C1, 32)));  // scope scratch
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
-  if (dry_ || !ok()) { launches_ += 2; return; }
+  if (dry_ || !ok()) { launches_ += groupnorm_launch_count(a); return; }
   begin_op(kCatGN);
-  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, 2);
+  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, groupnorm_launch_count(a));
 }
 
 void Builder::gemm(GemmArgs a, int cat) {

@@ -13,6 +13,8 @@
 // The input may be a channel concat [x0 ; x1] (up-block skip connections),
 // read in place from both sources. An image's result never depends on the
 // rest of the batch.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "sdg_kernels.h"
@@ -132,6 +134,141 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
   }
 }
 
+// Fused single-launch GroupNorm: an 8-CTA cluster per (channel slice, image).
+// Each CTA owns 1/8 of the image's pixels for a slice of whole groups; the
+// group sums (pass 1, mean) and centred sums of squares (pass 2, variance) are
+// exchanged through distributed shared memory and summed in rank order
+// (deterministic, exact); pass 3 normalises the CTA's chunk. Passes 2-3 re-read
+// the chunk, which is L2-resident. Rank 0 also records (mean, rstd) per group.
+constexpr int kGnClusterCtas = 8;
+constexpr int kGnFusedThreads = 256;
+
+__global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFusedThreads)
+    gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int slice = blockIdx.x / kGnClusterCtas;
+  const int img = blockIdx.y;
+  const int C = a.C0 + a.C1;
+  const int cpg = C / a.groups;
+  const int Ws = C / nslices;        // channels of this slice (whole groups, multiple of 8)
+  const int gps = Ws / cpg;          // groups in the slice
+  const int cbeg = slice * Ws;
+  const int nv = Ws / 8;
+  const int rows = kGnFusedThreads / nv;
+  const int chunk = (a.HW + kGnClusterCtas - 1) / kGnClusterCtas;
+  const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
+  const size_t img_base = (size_t)img * a.HW;
+  __shared__ float red[2048];        // [rows][Ws] per-channel partials (rows * Ws <= 2048)
+  __shared__ float part[2][32];      // per-group partials of this CTA, read by the whole cluster
+  __shared__ float gmu[32], grs[32];
+  __shared__ float sc[320], sh[320];
+  const int t = threadIdx.x;
+  const int v = t % nv, r = t / nv;
+  const bool active = r < rows;
+  const int c0 = cbeg + v * 8;       // first channel of this thread's vector
+  const float N = (float)a.HW * cpg;
+
+  auto reduce_to_groups = [&](const float (&acc)[8], int which) {
+    if (active) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red[r * Ws + v * 8 + e] = acc[e];
+    }
+    __syncthreads();
+    if (t < gps) {
+      float s = 0.f;
+      for (int rr = 0; rr < rows; ++rr)
+        for (int j = 0; j < cpg; ++j) s += red[rr * Ws + t * cpg + j];
+      part[which][t] = s;
+    }
+    cluster.sync();
+    if (t < gps) {
+      float s = 0.f;
+      for (int q = 0; q < kGnClusterCtas; ++q) s += cluster.map_shared_rank(&part[which][0], q)[t];
+      if (which == 0) gmu[t] = s / N;
+      else grs[t] = rsqrtf(s / N + a.eps);
+    }
+    __syncthreads();
+  };
+
+  // pass 1: sums
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  if (active) {
+    for (int pix = p0 + r; pix < p1; pix += rows) {
+      int cl;
+      const __half* src = gn_src(a, c0, img_base + pix, cl);
+      float x[8];
+      load8(src + cl, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += x[e];
+    }
+  }
+  reduce_to_groups(acc, 0);
+  // pass 2: centred squares
+  float mu[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) { acc[e] = 0.f; mu[e] = gmu[(v * 8 + e) / cpg]; }
+  if (active) {
+    for (int pix = p0 + r; pix < p1; pix += rows) {
+      int cl;
+      const __half* src = gn_src(a, c0, img_base + pix, cl);
+      float x[8];
+      load8(src + cl, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = x[e] - mu[e];
+        acc[e] += d * d;
+      }
+    }
+  }
+  reduce_to_groups(acc, 1);
+  if (rank == 0 && t < gps && gstat) gstat[img * a.groups + slice * gps + t] = make_float2(gmu[t], grs[t]);
+  for (int c = t; c < Ws; c += blockDim.x) {
+    const int g = c / cpg;
+    const float s = grs[g] * a.gamma[cbeg + c];
+    sc[c] = s;
+    sh[c] = a.beta[cbeg + c] - gmu[g] * s;
+  }
+  __syncthreads();
+  // pass 3: normalise this CTA's chunk
+  if (active) {
+    for (int pix = p0 + r; pix < p1; pix += rows) {
+      int cl;
+      const __half* src = gn_src(a, c0, img_base + pix, cl);
+      float x[8];
+      load8(src + cl, x);
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = v * 8 + 2 * e;
+        float y0 = x[2 * e] * sc[j] + sh[j];
+        float y1 = x[2 * e + 1] * sc[j + 1] + sh[j + 1];
+        if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
+        ow[e] = pack_half2(y0, y1);
+      }
+      *reinterpret_cast<uint4*>(a.y + (img_base + pix) * C + c0) = o;
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its `part`
+}
+
+// Largest slice count (dividing the group count) whose slice keeps whole
+// 8-channel vectors and at least 64 channels per pixel row; 0 if none fits.
+int gn_fused_slices(int C, int groups) {
+  int best = 0;
+  for (int ns = 1; ns <= groups; ns *= 2) {
+    if (groups % ns || C % ns) continue;
+    const int Ws = C / ns;
+    if (Ws % 8 || Ws > 320 || (Ws / 8) > kGnFusedThreads || (Ws % (C / groups))) continue;
+    if (Ws >= 64 || best == 0) best = ns;
+  }
+  return best;
+}
+
 // LayerNorm over C per token: one warp per token, values kept in registers,
 // exact centred variance. Replaces layernorm_f32.comp (vk_engine.cpp:652).
 template <int VPL>  // 8-channel vectors per lane
@@ -206,12 +343,21 @@ size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
   return (size_t)B * groups * sizeof(float2);
 }
 
+int groupnorm_launch_count(const GroupNormArgs& a) {
+  return (a.groups <= 32 && gn_fused_slices(a.C0 + a.C1, a.groups) > 0) ? 1 : 2;
+}
+
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
   const int C = a.C0 + a.C1;
   if (C <= 0 || C > kGnMaxC || C % 8 || a.C0 % 8 || (a.C1 && a.x1 == nullptr) || a.groups <= 0 || a.groups > 64 ||
       C % a.groups || (C / a.groups) % 2 || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
     return cudaErrorInvalidValue;
   float2* gstat = reinterpret_cast<float2*>(a.stats);
+  const int ns = a.groups <= 32 ? gn_fused_slices(C, a.groups) : 0;
+  if (ns > 0) {
+    gn_fused_kernel<<<dim3(ns * kGnClusterCtas, a.B), kGnFusedThreads, 0, s>>>(a, ns, gstat);
+    return cudaGetLastError();
+  }
   gn_stats_kernel<<<dim3(a.groups, a.B), kGnStatThreads, 0, s>>>(a, gstat);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

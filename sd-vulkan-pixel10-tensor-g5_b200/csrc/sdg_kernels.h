@@ -59,7 +59,8 @@ size_t gemm_workspace_bytes(const GemmArgs& a);
 int gemm_launch_count(const GemmArgs& a);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
-// tensors. stats: scratch of groupnorm_scratch_bytes() bytes (any contents).
+// tensors. stats: groupnorm_scratch_bytes() bytes; receives (mean, rstd) per
+// (image, group) as float2 [B][groups].
 struct GroupNormArgs {
   const __half* x0 = nullptr; const __half* x1 = nullptr;
   int C0 = 0, C1 = 0, B = 1, HW = 1, groups = 32;
@@ -70,6 +71,7 @@ struct GroupNormArgs {
 };
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s);
 size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups);
+int groupnorm_launch_count(const GroupNormArgs& a);
 
 cudaError_t launch_layernorm(const __half* x, int M, int C, const float* gamma, const float* beta, float eps,
                              __half* y, cudaStream_t s);

@@ -114,11 +114,15 @@ def test_unet_shared_timestep_and_tproj_entry(engine):
 
 
 def test_b2_selftest_semantics_and_cfg_entry(engine):
-    # vk_engine.cpp:823-839: the same input in both batch slots gives the B=1 output twice
+    # vk_engine.cpp:823-839: the same input in both batch slots gives the B=1 output twice.
+    # Inside one batch the two images take identical arithmetic (bit-identical); B=1 may
+    # pick another split-K partition, i.e. another fp32 summation order, so it agrees
+    # only to the fp16 noise floor (the parity bar).
     lat, t, ctx = W.make_inputs(1, 32, 32, seed=9)
     one = engine.forward(lat.numpy(), t.numpy(), ctx.numpy())
     both = engine.forward(np.repeat(lat.numpy(), 2, 0), np.repeat(t.numpy(), 2), np.repeat(ctx.numpy(), 2, 0))
-    assert rel(both[0], one[0]) < 1e-5 and rel(both[1], one[0]) < 1e-5
+    assert np.array_equal(both[0], both[1])
+    assert rel(both[0], one[0]) < UNET_TOL
     # unetForward2: [cond ; uncond] for one latent
     _, _, unc = W.make_inputs(1, 32, 32, seed=10)
     out2 = engine.forward_cfg(lat.numpy()[0], 999.0, ctx.numpy()[0], unc.numpy()[0])
