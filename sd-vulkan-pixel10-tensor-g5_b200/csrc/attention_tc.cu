@@ -11,12 +11,14 @@
 // 128-byte swizzle and both MMAs take K-major operands.
 // CTA = NQT query tiles of 128 rows of one (image, head):
 //   warp 0        TMA producer (Q once, K/V ring of NKV stages)
-//   warp 1        MMA issuer: S_t = Q_t K^T (TMEM), then O_t += P_t V
+//   warp 1        MMA issuer: S_t = Q_t K^T (TMEM), then PV_t = P_t V (TMEM)
 //   warps 2..     NQT softmax warpgroups, one TMEM row per thread: max,
-//                 exp2, row sum, fp16 P into swizzled smem (A operand of PV),
-//                 PV folded into register accumulators with the running
-//                 rescale, final 1/l and store.
-// Keys beyond Sk (cross-attention: 77 keys in a 128-key tile) are masked.
+//                 exp2, fp16 P into swizzled smem (A operand of PV), PV
+//                 folded into register accumulators with the running rescale.
+// When d < D16 (d = 40) row d of the V^T tile is set to ones in shared memory
+// (the TMA box loads only d rows), so PV column d is the row sum of the fp16
+// P actually used — the tensor core does the softmax denominators.
+// Keys beyond Sk (cross-attention: 77 keys) are masked in the last tile only.
 #include <algorithm>
 
 #include "sdg_kernels.h"
@@ -26,14 +28,17 @@
 namespace sdg {
 namespace {
 
-template <int DP_, int BKV_, int NQT_, int D16_>
+template <int DP_, int BKV_, int NQT_, int D16_, bool ONES_>
 struct AttnCfg {
   static constexpr int DP = DP_, BKV = BKV_, NQT = NQT_, D16 = D16_;
+  static constexpr bool ONES = ONES_;
   static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
-  static constexpr int NKV = (DP == 64) ? 3 : 2;              // K/V pipeline depth
+  static constexpr int NKATOM = BKV / 64;                     // 128B swizzle atoms along keys
+  static constexpr int NKV = (DP == 64) ? 4 : (DP == 128 ? 3 : 2);  // K/V pipeline depth
   static constexpr uint32_t kQTile = 128 * 128 * NATOM;       // bytes per 128-row Q tile
   static constexpr uint32_t kKTile = BKV * 128 * NATOM;       // bytes of K per stage
-  static constexpr uint32_t kVTile = (BKV / 64) * D16 * 128;   // bytes of V^T per stage
+  static constexpr uint32_t kVAtom = D16 * 128;               // bytes of one 64-key V^T atom
+  static constexpr uint32_t kVTile = NKATOM * kVAtom;         // bytes of V^T per stage
   static constexpr uint32_t kPTile = 128 * BKV * 2;           // fp16 P per query tile
   static constexpr int PVS = (D16 + 31) / 32 * 32;            // TMEM column stride of PV buffers
   static constexpr int kTmemNeed = NQT * BKV + NQT * PVS;
@@ -42,6 +47,7 @@ struct AttnCfg {
   static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)NQT * kPTile + 1024;
   static_assert(kSmem <= 232448, "attention tile configuration exceeds 227 KB of shared memory");
   static_assert(kTmemNeed <= 512, "attention tile configuration exceeds TMEM");
+  static_assert(kVAtom % 1024 == 0, "V^T atoms must stay 1024-byte aligned");
 };
 
 struct AttnDev {
@@ -57,6 +63,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                    const __grid_constant__ CUtensorMap map_v, const AttnDev p) {
   constexpr int BKV = CF::BKV, NQT = CF::NQT, NKV = CF::NKV, NATOM = CF::NATOM, D16 = CF::D16;
+  constexpr bool ONES = CF::ONES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -64,23 +71,24 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   uint8_t* sV = sK + NKV * CF::kKTile;
   uint8_t* sP = sV + NKV * CF::kVTile;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + NQT * CF::kPTile);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 64);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 96);
   const uint32_t b0 = smem_u32(bars);
   // barrier indices
   const uint32_t q_full = b0;
   auto kv_full = [&](int s) { return b0 + 8u * (1 + s); };
   auto kv_empty = [&](int s) { return b0 + 8u * (1 + NKV + s); };
   auto s_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + t); };
-  auto s_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 2 + t); };
-  auto p_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 + t); };
-  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 6 + t); };
-  auto pv_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 8 + t); };
-  const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 10);
+  auto s_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + NQT + t); };
+  auto p_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 2 * NQT + t); };
+  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 3 * NQT + t); };
+  auto pv_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 * NQT + t); };
+  const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 5 * NQT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
   const int q0 = blockIdx.x * 128 * NQT;
   const int nkv = (p.Sk + BKV - 1) / BKV;
+  const int vrows = ONES ? p.d : D16;  // rows of each V^T atom written by TMA
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -94,6 +102,19 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
+  }
+  if constexpr (ONES) {
+    // rows d..D16-1 of every V^T atom: row d = 1.0 (row-sum column of PV), the rest 0.
+    // TMA never writes these rows; the generic-proxy writes are fenced before any MMA.
+    const int extra = D16 - p.d;
+    const int per_stage = CF::NKATOM * extra * 8;  // 16-byte chunks
+    for (int i = threadIdx.x; i < NKV * per_stage; i += blockDim.x) {
+      const int s = i / per_stage, rem = i % per_stage;
+      const int a = rem / (extra * 8), rr = (rem / 8) % extra, ch = rem % 8;
+      const uint32_t v = (rr == 0) ? 0x3C003C00u : 0u;
+      *reinterpret_cast<uint4*>(sV + s * CF::kVTile + a * CF::kVAtom + (p.d + rr) * 128 + ch * 16) = make_uint4(v, v, v, v);
+    }
+    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), CF::kTmemCols);
@@ -117,17 +138,18 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       int last_ph[NKV];
       for (int s = 0; s < NKV; ++s) { issued[s] = false; last_ph[s] = 0; }
       bool ok = true;
+      const uint32_t kv_bytes = CF::kKTile + CF::NKATOM * vrows * 128;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % NKV;
         const uint32_t ph = (j / NKV) & 1;
         if (!mbar_wait(kv_empty(s), ph ^ 1u, p.err, kDevTimeoutAttn)) { ok = false; break; }
-        mbar_arrive_expect_tx(kv_full(s), CF::kKTile + CF::kVTile);
+        mbar_arrive_expect_tx(kv_full(s), kv_bytes);
         issued[s] = true;
         last_ph[s] = ph;
         for (int a = 0; a < NATOM; ++a)
           tma_load_3d(smem_u32(sK + s * CF::kKTile + a * BKV * 128), &map_k, kv_full(s), 64 * a, j * BKV, bh);
-        for (int a = 0; a < BKV / 64; ++a)
-          tma_load_3d(smem_u32(sV + s * CF::kVTile + a * D16 * 128), &map_v, kv_full(s), j * BKV + 64 * a, 0, bh);
+        for (int a = 0; a < CF::NKATOM; ++a)
+          tma_load_3d(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom), &map_v, kv_full(s), j * BKV + 64 * a, 0, bh);
       }
       if (!ok) {
         mbar_wait(q_full, 0, p.err, kDevTimeoutDrain);
@@ -140,9 +162,10 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       const uint32_t idesc_s = idesc_f16(128, BKV, false);
       const uint32_t idesc_o = idesc_f16(128, D16, false);
       bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn) && mbar_wait(kv_full(0), 0, p.err, kDevTimeoutAttn);
+      const int ksteps = (p.d + 15) / 16;  // QK^T depth: d rounded up to 16 (pads are zero)
       auto issue_qk = [&](int t, int s) {
         const uint32_t d_s = tmem + t * BKV;
-        for (int kk = 0; kk < D16 / 16; ++kk) {
+        for (int kk = 0; kk < ksteps; ++kk) {
           const int a = kk >> 2;
           const uint64_t da = sdesc_sw128(smem_u32(sQ + t * CF::kQTile + a * 16384) + (kk & 3) * 32, 16, 1024);
           const uint64_t db = sdesc_sw128(smem_u32(sK + s * CF::kKTile + a * BKV * 128) + (kk & 3) * 32, 16, 1024);
@@ -155,8 +178,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const int a = kk >> 2;
           const uint64_t da = sdesc_sw128(smem_u32(sP + t * CF::kPTile + a * 16384) + (kk & 3) * 32, 16, 1024);
-          // V^T tile: D16 rows (output dims) x 64 keys per atom, K-major over keys
-          const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * D16 * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom) + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(d_o, da, db, idesc_o, kk > 0 ? 1u : 0u);
         }
         mma_commit(pv_full(t));
@@ -210,15 +232,21 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int kbase = j * BKV;
+      const bool ragged = kbase + BKV > p.Sk;
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < BKV; c += 32) {
         uint32_t r[32];
         tmem_ld32(t_s + c, r);
         tmem_wait_ld();
+        if (!ragged) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (kbase + c + e < p.Sk) mx = fmaxf(mx, __uint_as_float(r[e]));
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (kbase + c + e < p.Sk) mx = fmaxf(mx, __uint_as_float(r[e]));
+        }
       }
       const float m_new = fmaxf(m, mx * p.sl2);
       const float corr = ex2_approx(m - m_new);
@@ -231,9 +259,13 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = (kbase + c + e < p.Sk) ? ex2_approx(__uint_as_float(r[e]) * p.sl2 - m_new) : 0.f;
-          const float p1 = (kbase + c + e + 1 < p.Sk) ? ex2_approx(__uint_as_float(r[e + 1]) * p.sl2 - m_new) : 0.f;
-          rs += p0 + p1;
+          float p0 = ex2_approx(fmaf(__uint_as_float(r[e]), p.sl2, -m_new));
+          float p1 = ex2_approx(fmaf(__uint_as_float(r[e + 1]), p.sl2, -m_new));
+          if (ragged) {
+            if (kbase + c + e >= p.Sk) p0 = 0.f;
+            if (kbase + c + e + 1 >= p.Sk) p1 = 0.f;
+          }
+          if constexpr (!ONES) rs += p0 + p1;
           pk[e >> 1] = pack_half2(p0, p1);
         }
         // 32 keys = four 16-byte chunks of the 128B-swizzled K-major row
@@ -250,7 +282,6 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       if (lane == 0) mbar_arrive(s_free(t));
       fence_proxy_async_smem();
       mbar_arrive(p_full(t));
-      l = l * corr + rs;
       m = m_new;
       ok = mbar_wait(pv_full(t), j & 1, p.err, kDevTimeoutAttn);
       ok = __all_sync(0xffffffffu, ok);
@@ -264,9 +295,16 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e) O[c + e] = O[c + e] * corr + __uint_as_float(r[e]);
       }
+      if constexpr (!ONES) l = l * corr + rs;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pv_free(t));
+    }
+    if constexpr (ONES) {
+      // column d of the PV accumulator is the running row sum (same rescaling as O)
+#pragma unroll
+      for (int c = 0; c < D16; ++c)
+        if (c == p.d) l = O[c];
     }
     const int qi = q0 + t * 128 + row;
     if (ok && qi < p.Sq) {
@@ -303,6 +341,7 @@ cudaError_t launch_cfg(const AttnArgs& a, int* err, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
+  if (CF::ONES && a.d >= CF::D16) return cudaErrorInvalidValue;
   CUtensorMap mq{}, mk{}, mv{};
   auto mk3 = [&](CUtensorMap* m, const __half* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
     uint64_t dims[3] = {inner, rows, (uint64_t)a.BH};
@@ -310,8 +349,9 @@ cudaError_t launch_cfg(const AttnArgs& a, int* err, cudaStream_t s) {
     uint32_t box[3] = {64, box_rows, 1};
     return make_tmap(m, base, 3, dims, str, box);
   };
+  const uint32_t vrows = CF::ONES ? (uint32_t)a.d : (uint32_t)CF::D16;
   if (!mk3(&mq, a.q, CF::DP, a.Sq, 128) || !mk3(&mk, a.k, CF::DP, a.Sk, CF::BKV) ||
-      !mk3(&mv, a.v, a.vt_ld, CF::D16, CF::D16))
+      !mk3(&mv, a.v, a.vt_ld, CF::D16, vrows))
     return cudaErrorInvalidValue;
   AttnDev d{a.heads, a.Sq, a.Sk, a.d, a.o, a.ld_o, a.scale * 1.4426950408889634f, err};
   dim3 grid((a.Sq + 128 * CF::NQT - 1) / (128 * CF::NQT), a.BH);
@@ -326,11 +366,15 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
     return cudaErrorInvalidValue;
   const int dp = (a.d + 63) / 64 * 64;
   if (a.dp != dp || a.vt_ld < a.Sk || a.vt_ld % 8 || a.d16 != (a.d + 15) / 16 * 16) return cudaErrorInvalidValue;
+  // few query tiles: fewer tiles per CTA keep more SMs busy
+  const bool small_q = (long)((a.Sq + 127) / 128) * a.BH < 2 * num_sms();
   switch (a.d16) {
-    case 48: return launch_cfg<AttnCfg<64, 128, 2, 48>>(a, err, s);
-    case 64: return launch_cfg<AttnCfg<64, 128, 2, 64>>(a, err, s);
-    case 80: return launch_cfg<AttnCfg<128, 128, 1, 80>>(a, err, s);
-    case 160: return launch_cfg<AttnCfg<192, 64, 1, 160>>(a, err, s);
+    case 48:
+      if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
+      return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);
+    case 64: return launch_cfg<AttnCfg<64, 64, 4, 64, false>>(a, err, s);
+    case 80: return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
+    case 160: return launch_cfg<AttnCfg<192, 64, 1, 160, false>>(a, err, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -135,13 +135,16 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
 }
 
 // Fused single-launch GroupNorm: an 8-CTA cluster per (channel slice, image).
-// Each CTA owns 1/8 of the image's pixels for a slice of whole groups; the
-// group sums (pass 1, mean) and centred sums of squares (pass 2, variance) are
-// exchanged through distributed shared memory and summed in rank order
-// (deterministic, exact); pass 3 normalises the CTA's chunk. Passes 2-3 re-read
-// the chunk, which is L2-resident. Rank 0 also records (mean, rstd) per group.
+// Each CTA owns 1/8 of the image's pixels for a slice of whole groups. Every
+// thread issues all loads of its share of the chunk up front (at most kGnMaxV
+// 16-byte vectors, kept in registers: high memory-level parallelism, one
+// global read per element). Group sums (pass 1, mean) and centred sums of
+// squares (pass 2, variance) are exchanged through distributed shared memory
+// and summed in rank order (deterministic, exact two-pass); pass 3 normalises
+// from registers. Rank 0 also records (mean, rstd) per group.
 constexpr int kGnClusterCtas = 8;
-constexpr int kGnFusedThreads = 256;
+constexpr int kGnFusedThreads = 512;
+constexpr int kGnMaxV = 16;
 
 __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFusedThreads)
     gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
@@ -160,7 +163,7 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
   const int chunk = (a.HW + kGnClusterCtas - 1) / kGnClusterCtas;
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
-  __shared__ float red[2048];        // [rows][Ws] per-channel partials (rows * Ws <= 2048)
+  __shared__ float red[4096];        // [rows][Ws] per-channel partials (rows * Ws <= 4096)
   __shared__ float part[2][32];      // per-group partials of this CTA, read by the whole cluster
   __shared__ float gmu[32], grs[32];
   __shared__ float sc[320], sh[320];
@@ -168,8 +171,26 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
   const int v = t % nv, r = t / nv;
   const bool active = r < rows;
   const int c0 = cbeg + v * 8;       // first channel of this thread's vector
+  const int cnt = (active && p0 + r < p1) ? (p1 - p0 - r + rows - 1) / rows : 0;
   const float N = (float)a.HW * cpg;
 
+  uint4 xs[kGnMaxV];
+  int cl;
+  const __half* src0 = gn_src(a, c0, img_base + p0 + r, cl);
+  const size_t pstride = (size_t)rows * (c0 < a.C0 ? a.C0 : a.C1);  // elements between a thread's pixels
+#pragma unroll
+  for (int i = 0; i < kGnMaxV; ++i)
+    if (i < cnt) xs[i] = *reinterpret_cast<const uint4*>(src0 + cl + i * pstride);
+
+  auto unpack = [](const uint4& u, float (&x)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __half22float2(h[e]);
+      x[2 * e] = f.x;
+      x[2 * e + 1] = f.y;
+    }
+  };
   auto reduce_to_groups = [&](const float (&acc)[8], int which) {
     if (active) {
 #pragma unroll
@@ -192,31 +213,27 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
     __syncthreads();
   };
 
-  // pass 1: sums
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  if (active) {
-    for (int pix = p0 + r; pix < p1; pix += rows) {
-      int cl;
-      const __half* src = gn_src(a, c0, img_base + pix, cl);
+#pragma unroll
+  for (int i = 0; i < kGnMaxV; ++i) {
+    if (i < cnt) {
       float x[8];
-      load8(src + cl, x);
+      unpack(xs[i], x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] += x[e];
     }
   }
   reduce_to_groups(acc, 0);
-  // pass 2: centred squares
   float mu[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) { acc[e] = 0.f; mu[e] = gmu[(v * 8 + e) / cpg]; }
-  if (active) {
-    for (int pix = p0 + r; pix < p1; pix += rows) {
-      int cl;
-      const __half* src = gn_src(a, c0, img_base + pix, cl);
+  for (int e = 0; e < 8; ++e) { acc[e] = 0.f; mu[e] = active ? gmu[(v * 8 + e) / cpg] : 0.f; }
+#pragma unroll
+  for (int i = 0; i < kGnMaxV; ++i) {
+    if (i < cnt) {
       float x[8];
-      load8(src + cl, x);
+      unpack(xs[i], x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float d = x[e] - mu[e];
@@ -233,24 +250,27 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
     sh[c] = a.beta[cbeg + c] - gmu[g] * s;
   }
   __syncthreads();
-  // pass 3: normalise this CTA's chunk
   if (active) {
-    for (int pix = p0 + r; pix < p1; pix += rows) {
-      int cl;
-      const __half* src = gn_src(a, c0, img_base + pix, cl);
-      float x[8];
-      load8(src + cl, x);
-      uint4 o;
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+    float scl[8], shf[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = v * 8 + 2 * e;
-        float y0 = x[2 * e] * sc[j] + sh[j];
-        float y1 = x[2 * e + 1] * sc[j + 1] + sh[j + 1];
-        if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
-        ow[e] = pack_half2(y0, y1);
+    for (int e = 0; e < 8; ++e) { scl[e] = sc[v * 8 + e]; shf[e] = sh[v * 8 + e]; }
+    __half* dst0 = a.y + (img_base + p0 + r) * C + c0;
+#pragma unroll
+    for (int i = 0; i < kGnMaxV; ++i) {
+      if (i < cnt) {
+        float x[8];
+        unpack(xs[i], x);
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float y0 = x[2 * e] * scl[2 * e] + shf[2 * e];
+          float y1 = x[2 * e + 1] * scl[2 * e + 1] + shf[2 * e + 1];
+          if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
+          ow[e] = pack_half2(y0, y1);
+        }
+        *reinterpret_cast<uint4*>(dst0 + (size_t)i * rows * C) = o;
       }
-      *reinterpret_cast<uint4*>(a.y + (img_base + pix) * C + c0) = o;
     }
   }
   cluster.sync();  // no CTA leaves while another may still read its `part`
@@ -258,12 +278,15 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
 
 // Largest slice count (dividing the group count) whose slice keeps whole
 // 8-channel vectors and at least 64 channels per pixel row; 0 if none fits.
-int gn_fused_slices(int C, int groups) {
+int gn_fused_slices(int C, int groups, int HW) {
   int best = 0;
+  const int chunk = (HW + kGnClusterCtas - 1) / kGnClusterCtas;
   for (int ns = 1; ns <= groups; ns *= 2) {
     if (groups % ns || C % ns) continue;
     const int Ws = C / ns;
-    if (Ws % 8 || Ws > 320 || (Ws / 8) > kGnFusedThreads || (Ws % (C / groups))) continue;
+    if (Ws % 8 || Ws > 320 || (Ws % (C / groups)) || Ws / (C / groups) > 32) continue;
+    const int rows = kGnFusedThreads / (Ws / 8);
+    if ((chunk + rows - 1) / rows > kGnMaxV) continue;  // the chunk must fit in registers
     if (Ws >= 64 || best == 0) best = ns;
   }
   return best;
@@ -344,7 +367,7 @@ size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
 }
 
 int groupnorm_launch_count(const GroupNormArgs& a) {
-  return (a.groups <= 32 && gn_fused_slices(a.C0 + a.C1, a.groups) > 0) ? 1 : 2;
+  return (a.groups <= 32 && gn_fused_slices(a.C0 + a.C1, a.groups, a.HW) > 0) ? 1 : 2;
 }
 
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
@@ -353,7 +376,7 @@ cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
       C % a.groups || (C / a.groups) % 2 || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
     return cudaErrorInvalidValue;
   float2* gstat = reinterpret_cast<float2*>(a.stats);
-  const int ns = a.groups <= 32 ? gn_fused_slices(C, a.groups) : 0;
+  const int ns = a.groups <= 32 ? gn_fused_slices(C, a.groups, a.HW) : 0;
   if (ns > 0) {
     gn_fused_kernel<<<dim3(ns * kGnClusterCtas, a.B), kGnFusedThreads, 0, s>>>(a, ns, gstat);
     return cudaGetLastError();
