@@ -164,6 +164,8 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
   __shared__ float red[4096];        // [rows][Ws] per-channel partials (rows * Ws <= 4096)
+  __shared__ float red2[kGnFusedThreads];  // [row slice][Ws] (slices * Ws <= threads)
+  __shared__ float chan[320];        // per-channel CTA sums
   __shared__ float part[2][32];      // per-group partials of this CTA, read by the whole cluster
   __shared__ float gmu[32], grs[32];
   __shared__ float sc[320], sh[320];
@@ -197,11 +199,27 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
       for (int e = 0; e < 8; ++e) red[r * Ws + v * 8 + e] = acc[e];
     }
     __syncthreads();
-    if (t < gps) {
+    // rows -> row slices (all threads), slices -> channels, channels -> groups (a warp per group);
+    // every sum in a fixed order (deterministic)
+    const int nslc = kGnFusedThreads / Ws;
+    if (t < nslc * Ws) {
+      const int c = t % Ws, rs = t / Ws;
       float s = 0.f;
-      for (int rr = 0; rr < rows; ++rr)
-        for (int j = 0; j < cpg; ++j) s += red[rr * Ws + t * cpg + j];
-      part[which][t] = s;
+      for (int rr = rs; rr < rows; rr += nslc) s += red[rr * Ws + c];
+      red2[rs * Ws + c] = s;
+    }
+    __syncthreads();
+    if (t < Ws) {
+      float s = 0.f;
+      for (int rs = 0; rs < nslc; ++rs) s += red2[rs * Ws + t];
+      chan[t] = s;
+    }
+    __syncthreads();
+    for (int g = t >> 5; g < gps; g += kGnFusedThreads / 32) {
+      float s = 0.f;
+      for (int j = (t & 31); j < cpg; j += 32) s += chan[g * cpg + j];
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if ((t & 31) == 0) part[which][g] = s;
     }
     cluster.sync();
     if (t < gps) {
