@@ -13,8 +13,8 @@
 //   warp 0        TMA producer (Q once, K/V ring of NKV stages)
 //   warp 1        MMA issuer: S_t = Q_t K^T (TMEM), then PV_t = P_t V (TMEM)
 //   warps 2..     NQT softmax warpgroups, one TMEM row per thread: max,
-//                 exp2, fp16 P into swizzled smem (A operand of PV), PV
-//                 folded into register accumulators with the running rescale.
+//                 exp2, fp16 P into swizzled smem (A operand of PV); O stays
+//                 in TMEM (PV accumulates), rescaled lazily per row.
 // When d < D16 (d = 40) row d of the V^T tile is set to ones in shared memory
 // (the TMA box loads only d rows), so PV column d is the row sum of the fp16
 // P actually used — the tensor core does the softmax denominators.
@@ -81,7 +81,6 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   auto s_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + NQT + t); };
   auto p_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 2 * NQT + t); };
   auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 3 * NQT + t); };
-  auto pv_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 * NQT + t); };
   const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 5 * NQT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -98,7 +97,6 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       mbar_init(s_free(t), 4);
       mbar_init(p_full(t), 128);
       mbar_init(pv_full(t), 1);
-      mbar_init(pv_free(t), 4);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -173,13 +171,13 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
         mma_commit(s_full(t));
       };
-      auto issue_pv = [&](int t, int s) {
+      auto issue_pv = [&](int t, int s, int j) {
         const uint32_t d_o = tmem + NQT * BKV + t * CF::PVS;
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const int a = kk >> 2;
           const uint64_t da = sdesc_sw128(smem_u32(sP + t * CF::kPTile + a * 16384) + (kk & 3) * 32, 16, 1024);
           const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom) + (kk & 3) * 32, 16, 1024);
-          mma_f16_ss(d_o, da, db, idesc_o, kk > 0 ? 1u : 0u);
+          mma_f16_ss(d_o, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(pv_full(t));
       };
@@ -200,9 +198,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
         for (int t = 0; t < NQT; ++t) {
           if (!mbar_wait(p_full(t), j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-          if (j > 0 && !mbar_wait(pv_free(t), (j - 1) & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(t, j % NKV);
+          issue_pv(t, j % NKV, j);
         }
         if (!ok) break;
         mma_commit(kv_empty(j % NKV));
@@ -212,6 +209,12 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax
+    // O accumulates in TMEM (PV with accumulate); a row's running max is only
+    // raised when a new score exceeds it by more than 2^8 (then that O row and l
+    // are rescaled through tcgen05.ld/st), so P <= 256 always fits fp16 and the
+    // per-tile path is: load S, max, exp2, store P.
+    static_assert(BKV == 64, "softmax path is written for 64-key tiles");
+    constexpr float kRescale = 8.f;
     const int sw = warp - 2;        // 0 .. 4*NQT-1
     const int t = sw >> 2;          // query tile of this warpgroup
     const int lg = warp & 3;        // TMEM lane group
@@ -221,105 +224,116 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     const uint32_t t_o = tmem + NQT * BKV + t * CF::PVS + lane_off;
     uint8_t* prow = sP + t * CF::kPTile + row * 128;
     const int r7 = row & 7;
-    float O[D16];
-#pragma unroll
-    for (int i = 0; i < D16; ++i) O[i] = 0.f;
-    float m = -INFINITY, l = 0.f;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       ok = mbar_wait(s_full(t), j & 1, p.err, kDevTimeoutAttn);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int kbase = j * BKV;
-      const bool ragged = kbase + BKV > p.Sk;
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_s + c, r);
-        tmem_wait_ld();
-        if (!ragged) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kbase + c + e < p.Sk) mx = fmaxf(mx, __uint_as_float(r[e]));
-        }
-      }
-      const float m_new = fmaxf(m, mx * p.sl2);
-      const float corr = ex2_approx(m - m_new);
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_s + c, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2_approx(fmaf(__uint_as_float(r[e]), p.sl2, -m_new));
-          float p1 = ex2_approx(fmaf(__uint_as_float(r[e + 1]), p.sl2, -m_new));
-          if (ragged) {
-            if (kbase + c + e >= p.Sk) p0 = 0.f;
-            if (kbase + c + e + 1 >= p.Sk) p1 = 0.f;
-          }
-          if constexpr (!ONES) rs += p0 + p1;
-          pk[e >> 1] = pack_half2(p0, p1);
-        }
-        // 32 keys = four 16-byte chunks of the 128B-swizzled K-major row
-        const int atom = c >> 6;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((c & 63) >> 3) + q;
-          uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(prow + atom * 16384 + ((chunk ^ r7) << 4)) = u;
-        }
-      }
+      uint32_t sa[32], sb[32];
+      tmem_ld32(t_s, sa);
+      tmem_ld32(t_s + 32, sb);
+      tmem_wait_ld();
+      // S is in registers: release its TMEM so QK^T of the next tile can start
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free(t));
+      const int kbase = j * BKV;
+      if (kbase + BKV > p.Sk) {  // ragged last tile: masked keys score -inf (exp2 -> 0)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (kbase + e >= p.Sk) sa[e] = __float_as_uint(-INFINITY);
+          if (kbase + 32 + e >= p.Sk) sb[e] = __float_as_uint(-INFINITY);
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fmaxf(__uint_as_float(sa[e]), __uint_as_float(sb[e])));
+      const float m_cand = mx * p.sl2;
+      const bool need = m_cand > m_used + kRescale;
+      const float m_new = need ? m_cand : m_used;
+      const float corr = need ? ex2_approx(m_used - m_new) : 1.f;
+      if (j > 0) {
+        // PV(j-1) has read P and written O before P / O are touched again
+        ok = mbar_wait(pv_full(t), (j - 1) & 1, p.err, kDevTimeoutAttn);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < D16; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(t_o + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+            tmem_st16(t_o + c, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      float rs = 0.f;
+      auto emit_half = [&](const uint32_t (&sv)[32], int q0c) {
+        // 32 keys -> four 16-byte chunks (chunk index q0c..q0c+3) of the 128B-swizzled K-major row
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = ex2_approx(fmaf(__uint_as_float(sv[e]), p.sl2, -m_new));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), p.sl2, -m_new));
+          if constexpr (!ONES) rs += x0 + x1;
+          pk[e >> 1] = pack_half2(x0, x1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(prow + (((q0c + q) ^ r7) << 4)) = u;
+        }
+      };
+      emit_half(sa, 0);
+      emit_half(sb, 4);
+      if constexpr (!ONES) l = l * corr + rs;
+      m_used = m_new;
       fence_proxy_async_smem();
+      tc_fence_before();
       mbar_arrive(p_full(t));
-      m = m_new;
-      ok = mbar_wait(pv_full(t), j & 1, p.err, kDevTimeoutAttn);
+    }
+    if (ok && nkv > 0) {
+      ok = mbar_wait(pv_full(t), (nkv - 1) & 1, p.err, kDevTimeoutAttn);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+    }
+    if (ok) {
       tc_fence_after();
+      float O[D16];
 #pragma unroll
       for (int c = 0; c < D16; c += 16) {
         uint32_t r[16];
         tmem_ld16(t_o + c, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) O[c + e] = O[c + e] * corr + __uint_as_float(r[e]);
+        for (int e = 0; e < 16; ++e) O[c + e] = __uint_as_float(r[e]);
       }
-      if constexpr (!ONES) l = l * corr + rs;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pv_free(t));
-    }
-    if constexpr (ONES) {
-      // column d of the PV accumulator is the running row sum (same rescaling as O)
+      if constexpr (ONES) {
+        // column d of the PV accumulator is the row sum of the fp16 P (same rescaling as O)
 #pragma unroll
-      for (int c = 0; c < D16; ++c)
-        if (c == p.d) l = O[c];
-    }
-    const int qi = q0 + t * 128 + row;
-    if (ok && qi < p.Sq) {
-      const float inv = 1.f / l;
-      const int b = bh / p.heads, h = bh % p.heads;
-      __half* dst = p.o + ((size_t)b * p.Sq + qi) * p.ld_o + (size_t)h * p.d;
+        for (int c = 0; c < D16; ++c)
+          if (c == p.d) l = O[c];
+      }
+      const int qi = q0 + t * 128 + row;
+      if (qi < p.Sq) {
+        const float inv = 1.f / l;
+        const int b = bh / p.heads, h = bh % p.heads;
+        __half* dst = p.o + ((size_t)b * p.Sq + qi) * p.ld_o + (size_t)h * p.d;
 #pragma unroll
-      for (int c = 0; c < D16; c += 8) {
-        if (c >= p.d) break;
-        uint4 u;
-        u.x = pack_half2(O[c + 0] * inv, O[c + 1] * inv);
-        u.y = pack_half2(O[c + 2] * inv, O[c + 3] * inv);
-        u.z = pack_half2(O[c + 4] * inv, O[c + 5] * inv);
-        u.w = pack_half2(O[c + 6] * inv, O[c + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + c) = u;
+        for (int c = 0; c < D16; c += 8) {
+          if (c >= p.d) break;
+          uint4 u;
+          u.x = pack_half2(O[c + 0] * inv, O[c + 1] * inv);
+          u.y = pack_half2(O[c + 2] * inv, O[c + 3] * inv);
+          u.z = pack_half2(O[c + 4] * inv, O[c + 5] * inv);
+          u.w = pack_half2(O[c + 6] * inv, O[c + 7] * inv);
+          *reinterpret_cast<uint4*>(dst + c) = u;
+        }
       }
     }
   }
@@ -371,8 +385,8 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
   switch (a.d16) {
     case 48:
       if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
-      return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);
-    case 64: return launch_cfg<AttnCfg<64, 64, 4, 64, false>>(a, err, s);
+      return launch_cfg<AttnCfg<64, 64, 3, 48, true>>(a, err, s);
+    case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
     case 80: return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
     case 160: return launch_cfg<AttnCfg<192, 64, 1, 160, false>>(a, err, s);
     default: return cudaErrorInvalidValue;

@@ -57,9 +57,10 @@ struct GemmDev {
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 160 ? 5 : (BN >= 128 ? 6 : 8));
   static constexpr uint32_t kBTileBytes = BN * BK * 2;
   static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
+  // as many stages as shared memory holds: TMA latency from L2 needs deep pipelines
+  static constexpr int kStages = (232448 - 1024 - 256) / kStageBytes > 12 ? 12 : (232448 - 1024 - 256) / kStageBytes;
   static constexpr int kAccStride = BN <= 16 ? 16 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
   static constexpr uint32_t kTmemCols = (2 * kAccStride) < 32 ? 32 : 2 * kAccStride;
   static constexpr int kChunk = BN >= 32 ? 32 : 16;

@@ -2,8 +2,9 @@
 
 The counterpart of the reference's on-device microbench (``sd/VulkanBench.kt:66-126``:
 matmul / conv / groupnorm / silu / attention at UNet shapes), run through the
-C-ABI op surface on one GPU. Each op is timed with CUDA events over ``--iters``
-launches after ``--warmup``; inputs are seeded (activations N(0,1), weights
+C-ABI op surface on one GPU. Each op is timed with CUDA events over one replay
+of a CUDA graph holding ``--iters`` launches (after ``--warmup`` eager
+launches), so host launch overhead is excluded; inputs are seeded (activations N(0,1), weights
 N(0, 0.02)), fp16, fp32 accumulation.
 
   python opbench.py                       # every op, JSON line each
@@ -79,6 +80,7 @@ def main():
     ap.add_argument("--op", default=None)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of a CUDA-graph replay")
     a = ap.parse_args()
     sdg = importlib.import_module(os.path.basename(HERE))
     dev = torch.device("cuda", 0)
@@ -92,10 +94,23 @@ def main():
         for _ in range(a.warmup):
             fn()
         torch.cuda.synchronize()
+        run = fn
+        if not a.eager:
+            # replay a captured graph of `iters` launches: device time without host launch gaps
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(a.iters):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            run = g.replay
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(a.iters):
-            fn()
+        if a.eager:
+            for _ in range(a.iters):
+                run()
+        else:
+            run()
         e1.record(stream)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000.0 / a.iters
