@@ -44,7 +44,7 @@ struct AttnCfg {
   static constexpr int kTmemNeed = NQT * BKV + NQT * PVS;
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
   static constexpr int kThreads = 64 + 128 * NQT;
-  static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)NQT * kPTile + 1024;
+  static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)2 * NQT * kPTile + 1024;
   static_assert(kSmem <= 232448, "attention tile configuration exceeds 227 KB of shared memory");
   static_assert(kTmemNeed <= 512, "attention tile configuration exceeds TMEM");
   static_assert(kVAtom % 1024 == 0, "V^T atoms must stay 1024-byte aligned");
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   uint8_t* sK = sQ + NQT * CF::kQTile;
   uint8_t* sV = sK + NKV * CF::kKTile;
   uint8_t* sP = sV + NKV * CF::kVTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + NQT * CF::kPTile);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * NQT * CF::kPTile);  // P double-buffered per tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 96);
   const uint32_t b0 = smem_u32(bars);
   // barrier indices
@@ -79,8 +79,10 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   auto kv_empty = [&](int s) { return b0 + 8u * (1 + NKV + s); };
   auto s_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + t); };
   auto s_free = [&](int t) { return b0 + 8u * (1 + 2 * NKV + NQT + t); };
-  auto p_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 2 * NQT + t); };
-  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 3 * NQT + t); };
+  // one P-ready barrier per (tile, P buffer): P(j) and P(j+2) share a barrier and P(j+2)
+  // cannot be written before PV(j) ran, so a barrier never runs two phases ahead
+  auto p_full = [&](int t, int buf) { return b0 + 8u * (1 + 2 * NKV + 2 * NQT + 2 * t + buf); };
+  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 * NQT + t); };
   const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 5 * NQT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -95,7 +97,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     for (int t = 0; t < NQT; ++t) {
       mbar_init(s_full(t), 1);
       mbar_init(s_free(t), 4);
-      mbar_init(p_full(t), 128);
+      mbar_init(p_full(t, 0), 128);
+      mbar_init(p_full(t, 1), 128);
       mbar_init(pv_full(t), 1);
     }
     mbar_init(drain, 1);
@@ -157,9 +160,10 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Event-driven issue: each query tile advances on its own barriers, so one slow
+      // softmax warpgroup never delays the tensor-core work of the others.
       const uint32_t idesc_s = idesc_f16(128, BKV, false);
       const uint32_t idesc_o = idesc_f16(128, D16, false);
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn) && mbar_wait(kv_full(0), 0, p.err, kDevTimeoutAttn);
       const int ksteps = (p.d + 15) / 16;  // QK^T depth: d rounded up to 16 (pads are zero)
       auto issue_qk = [&](int t, int s) {
         const uint32_t d_s = tmem + t * BKV;
@@ -173,36 +177,61 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       };
       auto issue_pv = [&](int t, int s, int j) {
         const uint32_t d_o = tmem + NQT * BKV + t * CF::PVS;
+        const uint8_t* pbuf = sP + (2 * t + (j & 1)) * CF::kPTile;
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const int a = kk >> 2;
-          const uint64_t da = sdesc_sw128(smem_u32(sP + t * CF::kPTile + a * 16384) + (kk & 3) * 32, 16, 1024);
+          const uint64_t da = sdesc_sw128(smem_u32(pbuf + a * 16384) + (kk & 3) * 32, 16, 1024);
           const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom) + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(d_o, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(pv_full(t));
       };
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < NQT; ++t) issue_qk(t, 0);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv) {
-          const int s1 = (j + 1) % NKV;
-          if (!mbar_wait(kv_full(s1), ((j + 1) / NKV) & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-          for (int t = 0; t < NQT; ++t) {
-            if (!mbar_wait(s_free(t), j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
-            tc_fence_after();
-            issue_qk(t, s1);
-          }
-          if (!ok) break;
-        }
-        for (int t = 0; t < NQT; ++t) {
-          if (!mbar_wait(p_full(t), j & 1, p.err, kDevTimeoutAttn)) { ok = false; break; }
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
+      int nq[NQT], np[NQT];
+      for (int t = 0; t < NQT; ++t) { nq[t] = 0; np[t] = 0; }
+      int kv_loaded = 0, kv_released = 0;
+      uint64_t t_last = globaltimer();
+      uint32_t spins = 0;
+      while (ok) {
+        bool progress = false;
+        if (kv_loaded < nkv && mbar_test(kv_full(kv_loaded % NKV), (kv_loaded / NKV) & 1)) {
+          ++kv_loaded;
+          progress = true;
           tc_fence_after();
-          issue_pv(t, j % NKV, j);
         }
-        if (!ok) break;
-        mma_commit(kv_empty(j % NKV));
+        int min_np = nkv;
+#pragma unroll
+        for (int t = 0; t < NQT; ++t) {
+          // S buffer of tile t is free once the softmax released S(nq-1)
+          if (nq[t] < kv_loaded && (nq[t] == 0 || mbar_test(s_free(t), (nq[t] - 1) & 1))) {
+            tc_fence_after();
+            issue_qk(t, nq[t] % NKV);
+            ++nq[t];
+            progress = true;
+          }
+          if (np[t] < nq[t] && mbar_test(p_full(t, np[t] & 1), (np[t] >> 1) & 1)) {
+            tc_fence_after();
+            issue_pv(t, np[t] % NKV, np[t]);
+            ++np[t];
+            progress = true;
+          }
+          min_np = min(min_np, np[t]);
+        }
+        while (kv_released < min_np) {  // every tile's QK and PV of this K/V stage issued
+          mma_commit(kv_empty(kv_released % NKV));
+          ++kv_released;
+        }
+        if (kv_released == nkv) break;
+        if (progress) {
+          t_last = globaltimer();
+          spins = 0;
+        } else if ((++spins & 255u) == 0u) {
+          if (*reinterpret_cast<volatile int*>(p.err) != 0) ok = false;
+          else if (globaltimer() - t_last > kWaitTimeoutNs) {
+            atomicCAS(p.err, 0, kDevTimeoutAttn);
+            ok = false;
+          }
+        }
       }
       mma_commit(drain);
       mbar_wait(drain, 0, p.err, kDevTimeoutDrain);
@@ -222,10 +251,15 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(lg * 32) << 16;
     const uint32_t t_s = tmem + t * BKV + lane_off;
     const uint32_t t_o = tmem + NQT * BKV + t * CF::PVS + lane_off;
-    uint8_t* prow = sP + t * CF::kPTile + row * 128;
     const int r7 = row & 7;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    int pv_seen = 0;  // PV completions observed (phases of pv_full(t), taken in order)
+    auto wait_pv = [&](int k) -> bool {  // PV(k) complete
+      for (; pv_seen <= k; ++pv_seen)
+        if (!mbar_wait(pv_full(t), pv_seen & 1, p.err, kDevTimeoutAttn)) return false;
+      return true;
+    };
     for (int j = 0; j < nkv; ++j) {
       ok = mbar_wait(s_full(t), j & 1, p.err, kDevTimeoutAttn);
       ok = __all_sync(0xffffffffu, ok);
@@ -254,13 +288,14 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       const bool need = m_cand > m_used + kRescale;
       const float m_new = need ? m_cand : m_used;
       const float corr = need ? ex2_approx(m_used - m_new) : 1.f;
-      if (j > 0) {
-        // PV(j-1) has read P and written O before P / O are touched again
-        ok = mbar_wait(pv_full(t), (j - 1) & 1, p.err, kDevTimeoutAttn);
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, need);
+      if (rescale || j >= 2) {
+        // P buffer j%2 was read by PV(j-2); an O rescale needs PV(j-1) retired as well
+        ok = wait_pv(rescale ? j - 1 : j - 2);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
+        if (rescale) {
 #pragma unroll
           for (int c = 0; c < D16; c += 16) {
             uint32_t r[16];
@@ -274,6 +309,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
       }
       float rs = 0.f;
+      uint8_t* prow = sP + (2 * t + (j & 1)) * CF::kPTile + row * 128;
       auto emit_half = [&](const uint32_t (&sv)[32], int q0c) {
         // 32 keys -> four 16-byte chunks (chunk index q0c..q0c+3) of the 128B-swizzled K-major row
         uint32_t pk[16];
@@ -296,10 +332,10 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       m_used = m_new;
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full(t));
+      mbar_arrive(p_full(t, j & 1));
     }
     if (ok && nkv > 0) {
-      ok = mbar_wait(pv_full(t), (nkv - 1) & 1, p.err, kDevTimeoutAttn);
+      ok = wait_pv(nkv - 1);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
