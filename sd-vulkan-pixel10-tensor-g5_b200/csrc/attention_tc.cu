@@ -82,8 +82,10 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   // one P-ready barrier per (tile, P buffer): P(j) and P(j+2) share a barrier and P(j+2)
   // cannot be written before PV(j) ran, so a barrier never runs two phases ahead
   auto p_full = [&](int t, int buf) { return b0 + 8u * (1 + 2 * NKV + 2 * NQT + 2 * t + buf); };
-  auto pv_full = [&](int t) { return b0 + 8u * (1 + 2 * NKV + 4 * NQT + t); };
-  const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 5 * NQT);
+  // likewise one PV-done barrier per P buffer: PV(j) commits to pv_full(t, j & 1), so a
+  // waiter on PV(j-2) or PV(j-1) never finds its barrier two phases ahead
+  auto pv_full = [&](int t, int buf) { return b0 + 8u * (1 + 2 * NKV + 4 * NQT + 2 * t + buf); };
+  const uint32_t drain = b0 + 8u * (1 + 2 * NKV + 6 * NQT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -99,7 +101,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       mbar_init(s_free(t), 4);
       mbar_init(p_full(t, 0), 128);
       mbar_init(p_full(t, 1), 128);
-      mbar_init(pv_full(t), 1);
+      mbar_init(pv_full(t, 0), 1);
+      mbar_init(pv_full(t, 1), 1);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
           const uint64_t db = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom) + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(d_o, da, db, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(pv_full(t));
+        mma_commit(pv_full(t, j & 1));
       };
       bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutAttn);
       int nq[NQT], np[NQT];
@@ -254,11 +257,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     const int r7 = row & 7;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    int pv_seen = 0;  // PV completions observed (phases of pv_full(t), taken in order)
-    auto wait_pv = [&](int k) -> bool {  // PV(k) complete
-      for (; pv_seen <= k; ++pv_seen)
-        if (!mbar_wait(pv_full(t), pv_seen & 1, p.err, kDevTimeoutAttn)) return false;
-      return true;
+    auto wait_pv = [&](int k) -> bool {  // PV(k) complete: phase k>>1 of barrier k&1
+      return mbar_wait(pv_full(t, k & 1), (k >> 1) & 1, p.err, kDevTimeoutAttn);
     };
     for (int j = 0; j < nkv; ++j) {
       ok = mbar_wait(s_full(t), j & 1, p.err, kDevTimeoutAttn);
