@@ -134,17 +134,17 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
   }
 }
 
-// Fused single-launch GroupNorm: an 8-CTA cluster per (channel slice, image).
-// Each CTA owns 1/8 of the image's pixels for a slice of whole groups. Every
+// Fused single-launch GroupNorm: a 16-CTA cluster per (channel slice, image).
+// Each CTA owns 1/16 of the image's pixels for a slice of whole groups. Every
 // thread issues all loads of its share of the chunk up front (at most kGnMaxV
 // 16-byte vectors, kept in registers: high memory-level parallelism, one
 // global read per element). Group sums (pass 1, mean) and centred sums of
 // squares (pass 2, variance) are exchanged through distributed shared memory
 // and summed in rank order (deterministic, exact two-pass); pass 3 normalises
 // from registers. Rank 0 also records (mean, rstd) per group.
-constexpr int kGnClusterCtas = 8;
+constexpr int kGnClusterCtas = 16;  // non-portable size, opted in at launch
 constexpr int kGnFusedThreads = 512;
-constexpr int kGnMaxV = 16;
+constexpr int kGnMaxV = 8;
 
 __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFusedThreads)
     gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
@@ -395,6 +395,14 @@ cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   float2* gstat = reinterpret_cast<float2*>(a.stats);
   const int ns = a.groups <= 32 ? gn_fused_slices(C, a.groups, a.HW) : 0;
+  static bool cluster_ok[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (ns > 0 && dev < 64 && !cluster_ok[dev]) {
+    if (cudaFuncSetAttribute(gn_fused_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      return cudaErrorInvalidValue;
+    cluster_ok[dev] = true;
+  }
   if (ns > 0) {
     gn_fused_kernel<<<dim3(ns * kGnClusterCtas, a.B), kGnFusedThreads, 0, s>>>(a, ns, gstat);
     return cudaGetLastError();

@@ -204,7 +204,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) 
 }
 
 // ------------------------------------------------------------------ small math
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
