@@ -134,24 +134,26 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
   }
 }
 
-// Fused single-launch GroupNorm: a 16-CTA cluster per (channel slice, image).
-// Each CTA owns 1/16 of the image's pixels for a slice of whole groups. Every
+// Fused single-launch GroupNorm: a cluster of K CTAs (K = 1..16, chosen per
+// launch from the work: ~40 KB of input per CTA) per (channel slice, image).
+// Each CTA owns 1/K of the image's pixels for a slice of whole groups. Every
 // thread issues all loads of its share of the chunk up front (at most kGnMaxV
 // 16-byte vectors, kept in registers: high memory-level parallelism, one
 // global read per element). Group sums (pass 1, mean) and centred sums of
 // squares (pass 2, variance) are exchanged through distributed shared memory
 // and summed in rank order (deterministic, exact two-pass); pass 3 normalises
 // from registers. Rank 0 also records (mean, rstd) per group.
-constexpr int kGnClusterCtas = 16;  // non-portable size, opted in at launch
+constexpr int kGnMaxCluster = 16;  // non-portable size, opted in at launch
 constexpr int kGnFusedThreads = 512;
 constexpr int kGnMaxV = 8;
 
-__global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFusedThreads)
+__global__ void __launch_bounds__(kGnFusedThreads)
     gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int slice = blockIdx.x / kGnClusterCtas;
+  const int kc = (int)cluster.num_blocks();
+  const int slice = blockIdx.x / kc;
   const int img = blockIdx.y;
   const int C = a.C0 + a.C1;
   const int cpg = C / a.groups;
@@ -160,7 +162,7 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
   const int cbeg = slice * Ws;
   const int nv = Ws / 8;
   const int rows = kGnFusedThreads / nv;
-  const int chunk = (a.HW + kGnClusterCtas - 1) / kGnClusterCtas;
+  const int chunk = (a.HW + kc - 1) / kc;
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
   __shared__ float red[4096];        // [rows][Ws] per-channel partials (rows * Ws <= 4096)
@@ -224,7 +226,7 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
     cluster.sync();
     if (t < gps) {
       float s = 0.f;
-      for (int q = 0; q < kGnClusterCtas; ++q) s += cluster.map_shared_rank(&part[which][0], q)[t];
+      for (int q = 0; q < kc; ++q) s += cluster.map_shared_rank(&part[which][0], q)[t];
       if (which == 0) gmu[t] = s / N;
       else grs[t] = rsqrtf(s / N + a.eps);
     }
@@ -294,17 +296,29 @@ __global__ void __cluster_dims__(kGnClusterCtas, 1, 1) __launch_bounds__(kGnFuse
   cluster.sync();  // no CTA leaves while another may still read its `part`
 }
 
+// Cluster size for a (slice, image): ~40 KB of input per CTA, at most 16, and
+// small enough that each thread's share of the chunk fits kGnMaxV vectors.
+int gn_cluster_ctas(int HW, int Ws) {
+  const int rows = kGnFusedThreads / (Ws / 8);
+  const long bytes = (long)HW * Ws * 2;
+  int k = (int)std::min<long>(kGnMaxCluster, std::max<long>(1, (bytes + 40959) / 40960));
+  int pow2 = 1;
+  while (pow2 < k) pow2 *= 2;
+  k = pow2;
+  while (k <= kGnMaxCluster && ((HW + k - 1) / k + rows - 1) / rows > kGnMaxV) k *= 2;
+  return k <= kGnMaxCluster ? k : 0;
+}
+
 // Largest slice count (dividing the group count) whose slice keeps whole
-// 8-channel vectors and at least 64 channels per pixel row; 0 if none fits.
+// 8-channel vectors and at least 64 channels per pixel row and fits a cluster;
+// 0 if none fits.
 int gn_fused_slices(int C, int groups, int HW) {
   int best = 0;
-  const int chunk = (HW + kGnClusterCtas - 1) / kGnClusterCtas;
   for (int ns = 1; ns <= groups; ns *= 2) {
     if (groups % ns || C % ns) continue;
     const int Ws = C / ns;
     if (Ws % 8 || Ws > 320 || (Ws % (C / groups)) || Ws / (C / groups) > 32) continue;
-    const int rows = kGnFusedThreads / (Ws / 8);
-    if ((chunk + rows - 1) / rows > kGnMaxV) continue;  // the chunk must fit in registers
+    if (gn_cluster_ctas(HW, Ws) == 0) continue;
     if (Ws >= 64 || best == 0) best = ns;
   }
   return best;
@@ -404,8 +418,20 @@ cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
     cluster_ok[dev] = true;
   }
   if (ns > 0) {
-    gn_fused_kernel<<<dim3(ns * kGnClusterCtas, a.B), kGnFusedThreads, 0, s>>>(a, ns, gstat);
-    return cudaGetLastError();
+    const int kc = gn_cluster_ctas(a.HW, C / ns);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ns * kc, a.B);
+    cfg.blockDim = dim3(kGnFusedThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kc;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gn_fused_kernel, a, ns, gstat);
   }
   gn_stats_kernel<<<dim3(a.groups, a.B), kGnStatThreads, 0, s>>>(a, gstat);
   cudaError_t e = cudaGetLastError();
