@@ -29,6 +29,8 @@ from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
+from . import multigpu  # noqa: E402,F401  (batch sharding + latent gather across GPUs)
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsdg.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "sdg.h")
