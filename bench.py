@@ -96,11 +96,13 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_engine(sdg, device):
+def make_engine(sdg, device, wo8=False):
     from oracle import weights as Wt
     w = Wt.make_weights(0)
     eng = sdg.Engine(device)
     eng.upload_weights(Wt.iter_reference_blobs(w))
+    if wo8:
+        eng.quantize_wo8()
     eng.prepare()
     return eng, w
 
@@ -161,8 +163,11 @@ def run_reference_arm(args):
     return 0
 
 
-def config_dict(n):
-    return {"workload": "SD1.5 UNet forward, B=2 CFG pair, 64x64 latent, 77x768 context, t=999 (BASELINE config 0)",
+def config_dict(n, wo8=False):
+    wl = "SD1.5 UNet forward, B=2 CFG pair, 64x64 latent, 77x768 context, t=999 (BASELINE config 0)"
+    if wo8:
+        wl = wl.replace("config 0)", "config 4: weight-only int8, per-output-channel scales)")
+    return {"workload": wl,
             "global_batch": 2 * n, "latent": [H, W], "context": [77, 768], "parallelism": f"dp{n} (weights replicated)",
             "l2": "256 MB L2 flush (memset) between timed steps, outside the timed events; weights 1.72 GB > L2"}
 
@@ -174,6 +179,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--wo8", action="store_true", help="weight-only int8 engine (BASELINE config 4)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
@@ -190,7 +196,7 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    eng, wts = make_engine(sdg, local)
+    eng, wts = make_engine(sdg, local, args.wo8)
     from oracle import weights as Wt
     lat, t, ctx = Wt.make_inputs(B, H, W, seed=rank)
     d_lat, d_t, d_ctx = lat.to(dev), t.to(dev), ctx.to(dev)
@@ -283,8 +289,9 @@ def main():
         print(json.dumps({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded inputs, seeded default-init weights)",
-            "config": config_dict(world), "clocks": clk, "roofline": roofline, "cpu_baseline": cpu,
+            "vs_baseline": None, "dtype": "fp16 (int8 weights)" if args.wo8 else "fp16",
+            "data": "synthetic (seeded inputs, seeded default-init weights)",
+            "config": config_dict(world, args.wo8), "clocks": clk, "roofline": roofline, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches * args.steps,
             "tensor_peak_frac": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_burst,

@@ -72,6 +72,17 @@ SDG_API int sdg_load_dir(sdg_engine* e, const char* dir);
  * Returns SDG_ERR_MISSING_WEIGHT naming the first absent key. */
 SDG_API int sdg_prepare(sdg_engine* e);
 
+/* Switch the engine to weight-only int8 before it is prepared (BASELINE
+ * config 4; the reference's wo8 model, tools/quantize_wo8.py:42-46 with
+ * ai-edge-quantizer's weight_only_wi8_afp32 recipe). At preparation every
+ * conv and linear weight is quantized per output channel, symmetric, narrow
+ * range: scale = fp16(max|w| / 127) (1 for an all-zero row),
+ * q = clamp(round_half_even(w / scale), -127, 127). GEMMs then stream int8
+ * tiles and widen them to fp16 in shared memory (dequantised in the
+ * mainloop); norms, biases and activations stay as in the fp16 path.
+ * SDG_ERR_ARG if the engine is already prepared. */
+SDG_API int sdg_quantize_wo8(sdg_engine* e);
+
 /* Replaces Java_..._unetRelease (vk_engine.cpp:915-926): frees everything. */
 SDG_API int sdg_release(sdg_engine* e);
 
@@ -151,6 +162,17 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
 SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
                        const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
                        int* err_word, void* stream);
+
+/* sdg_linear with weight-only int8 weights: w8 [N,K] int8 and wscale [N] fp32
+ * (per output row; the weight is w8[n,k] * wscale[n]). The int8 tile is
+ * widened to fp16 in shared memory inside the GEMM mainloop and the scale is
+ * applied to the fp32 accumulator in the epilogue. Same act / GEGLU layout /
+ * residual / workspace rules as sdg_linear. Replaces the reference's wo8
+ * model path (tools/quantize_wo8.py:42-46, weight_only_wi8_afp32), which has
+ * no op-level entry of its own. */
+SDG_API int sdg_linear_wo8(const uint16_t* x, int M, int K, const int8_t* w8, const float* wscale, const float* bias,
+                           int N, const uint16_t* residual, int act, uint16_t* y, void* workspace,
+                           size_t workspace_bytes, int* err_word, void* stream);
 
 /* GroupNorm(groups) (+SiLU) over x (optionally channel-concat [x ; x2]),
  * [B,HW,C1+C2] -> y. stats_scratch: device memory of at least

@@ -62,6 +62,7 @@ _SIGS = {
     "sdg_upload_weight": (_I, [_P, ctypes.c_char_p, _P, ctypes.POINTER(ctypes.c_int64), _I]),
     "sdg_load_dir": (_I, [_P, ctypes.c_char_p]),
     "sdg_prepare": (_I, [_P]),
+    "sdg_quantize_wo8": (_I, [_P]),
     "sdg_release": (_I, [_P]),
     "sdg_last_error": (_I, [ctypes.c_char_p, _I]),
     "sdg_unet_forward": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
@@ -74,6 +75,7 @@ _SIGS = {
     "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, ctypes.c_size_t, _P,
                         _P]),
     "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
+    "sdg_linear_wo8": (_I, [_P, _I, _I, _P, _P, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
     "sdg_groupnorm": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P, _P]),
     "sdg_groupnorm_scratch_bytes": (ctypes.c_size_t, [_I, _I, _I, _I]),
     "sdg_groupnorm_noalloc": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _F, _I, _P, _P]),
@@ -167,6 +169,11 @@ class Engine:
 
     def prepare(self) -> None:
         check(lib().sdg_prepare(self._h))
+
+    def quantize_wo8(self) -> None:
+        """Use weight-only int8 weights (per output channel, scale fp16(max|w|/127));
+        must precede ``prepare`` / the first forward."""
+        check(lib().sdg_quantize_wo8(self._h))
 
     # forward -------------------------------------------------------------
     def forward(self, latent: np.ndarray, timesteps, context: np.ndarray) -> np.ndarray:
@@ -271,6 +278,32 @@ def linear(x, w, bias=None, residual=None, act: int = 0, out=None, workspace=Non
     check(lib().sdg_linear(_ptr(x), M, K, _ptr(w), _ptr(bias), N, _ptr(residual), act, _ptr(out), _ptr(workspace),
                            wsb, _ptr(err_word), _stream(stream)))
     return out
+
+
+def linear_wo8(x, w8, wscale, bias=None, residual=None, act: int = 0, out=None, workspace=None, err_word=None,
+               stream=None):
+    """x [M,K] fp16, w8 [N,K] int8, wscale [N] fp32 -> [M,N] fp16 (weight = w8 * wscale per row)."""
+    import torch
+    M, K = x.shape
+    N = w8.shape[0]
+    if out is None:
+        out = torch.empty((M, N // 2 if act == 2 else N), dtype=torch.float16, device=x.device)
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().sdg_linear_wo8(_ptr(x), M, K, _ptr(w8), _ptr(wscale), _ptr(bias), N, _ptr(residual), act, _ptr(out),
+                               _ptr(workspace), wsb, _ptr(err_word), _stream(stream)))
+    return out
+
+
+def quantize_wo8_rows(w):
+    """Per-row symmetric int8 of a [N,K] weight (torch tensor): (q int8, scale fp32), the
+    same rule the engine applies (scale = fp16(max|w|/127), 1 for a zero row,
+    q = clamp(round_half_even(w/scale), +-127))."""
+    import torch
+    wf = w.float()
+    s = (wf.abs().amax(dim=1) / 127.0).half().float()
+    s = torch.where(s == 0, torch.ones_like(s), s)
+    q = torch.clamp(torch.round(wf / s[:, None]), -127, 127).to(torch.int8)
+    return q, s
 
 
 def groupnorm(x, gamma, beta, eps: float, silu: bool, x2=None, groups: int = 32, out=None, stats=None, stream=None):

@@ -116,27 +116,46 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
   return cuda_status(sdg::launch_gemm(a, err, s), "conv2d");
 }
 
-SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
-                       const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
-                       int* err_word, void* stream) {
-  if (!x || !w || !y || M <= 0 || K <= 0 || N <= 0) return sdg::op_fail(SDG_ERR_ARG, "linear: bad arguments");
+static int linear_common(const char* name, const uint16_t* x, int M, int K, const uint16_t* w, const int8_t* w8,
+                         const float* wscale, const float* bias, int N, const uint16_t* residual, int act, uint16_t* y,
+                         void* workspace, size_t workspace_bytes, int* err_word, void* stream) {
+  if (!x || !(w || (w8 && wscale)) || !y || M <= 0 || K <= 0 || N <= 0)
+    return sdg::op_fail(SDG_ERR_ARG, std::string(name) + ": bad arguments");
   sdg::GemmArgs a;
   a.M = M; a.N = N; a.K = K; a.taps = 1;
   a.a0 = reinterpret_cast<const __half*>(x); a.cin0 = K;
   a.w = reinterpret_cast<const __half*>(w);
+  a.w8 = w8;
+  a.wscale = wscale;
   a.bias = bias;
   a.residual = reinterpret_cast<const __half*>(residual);
   a.out = reinterpret_cast<__half*>(y);
   a.ws = static_cast<float*>(workspace);
   a.ws_bytes = workspace ? workspace_bytes : 0;
   if (act == 2) {
-    if (residual) return sdg::op_fail(SDG_ERR_ARG, "linear: GEGLU takes no residual");
+    if (residual) return sdg::op_fail(SDG_ERR_ARG, std::string(name) + ": GEGLU takes no residual");
     a.epi = sdg::kEpiGeglu;
   } else {
     a.act = act == 1 ? 1 : 0;
   }
   int* err = err_word ? err_word : internal_err_word();
-  return cuda_status(sdg::launch_gemm(a, err, static_cast<cudaStream_t>(stream)), "linear");
+  return cuda_status(sdg::launch_gemm(a, err, static_cast<cudaStream_t>(stream)), name);
+}
+
+SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
+                       const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
+                       int* err_word, void* stream) {
+  if (!w) return sdg::op_fail(SDG_ERR_ARG, "linear: bad arguments");
+  return linear_common("linear", x, M, K, w, nullptr, nullptr, bias, N, residual, act, y, workspace,
+                       workspace_bytes, err_word, stream);
+}
+
+SDG_API int sdg_linear_wo8(const uint16_t* x, int M, int K, const int8_t* w8, const float* wscale, const float* bias,
+                           int N, const uint16_t* residual, int act, uint16_t* y, void* workspace,
+                           size_t workspace_bytes, int* err_word, void* stream) {
+  if (!w8 || !wscale) return sdg::op_fail(SDG_ERR_ARG, "linear_wo8: bad arguments");
+  return linear_common("linear_wo8", x, M, K, nullptr, w8, wscale, bias, N, residual, act, y, workspace,
+                       workspace_bytes, err_word, stream);
 }
 
 SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,

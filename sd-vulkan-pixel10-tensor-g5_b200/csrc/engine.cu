@@ -53,9 +53,12 @@ struct HostWeight {
   std::vector<uint16_t> data;
   std::vector<int64_t> shape;
 };
-struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; };
+// fp16 weights (w), or weight-only int8 (w8 + per-row scale ws) after sdg_quantize_wo8
+struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; int8_t* w8 = nullptr; float* ws = nullptr; };
 struct Norm { float* g = nullptr; float* b = nullptr; int C = 0; };
-struct ConvW { __half* w = nullptr; float* b = nullptr; int Co = 0, Ci = 0, k = 3; };
+struct ConvW {
+  __half* w = nullptr; float* b = nullptr; int Co = 0, Ci = 0, k = 3; int8_t* w8 = nullptr; float* ws = nullptr;
+};
 struct ResW { Norm n1, n2; ConvW c1, c2; bool has_sc = false; Lin sc; int tp_off = 0, cin = 0, cout = 0; };
 struct TfW { Norm gn, ln1, ln2, ln3; Lin pin, qkv, out1, q2, kv2, out2, ff1, ff2, pout; int C = 0; };
 struct UNetW {
@@ -71,6 +74,8 @@ struct UNetW {
   TfW up_tf[4][3];  // [0][*] unused
   ConvW up_us[3];
   __half* tp_w = nullptr;
+  int8_t* tp_w8 = nullptr;
+  float* tp_ws = nullptr;
   float* tp_b = nullptr;
   int tp_N = 0;
 };
@@ -158,6 +163,7 @@ struct Engine {
   cudaStream_t stream = nullptr;
   std::unordered_map<std::string, HostWeight> host;
   bool prepared = false;
+  bool wo8 = false;  // weight-only int8 (set by sdg_quantize_wo8 before preparation)
   char* warena = nullptr;
   size_t warena_bytes = 0;
   UNetW w;
@@ -184,8 +190,49 @@ struct WeightPacker {
   std::vector<char> staging;  // host image of the device weight arena
   size_t off = 0;
   std::vector<std::pair<size_t, void**>> fixups;
+  struct Mat {  // a packed [rows][cols] fp16 weight matrix (quantized in place for wo8)
+    size_t off, scale_off;
+    int rows, cols;
+    __half** w16;
+    int8_t** w8;
+  };
+  std::vector<Mat> mats;
   std::string missing;
   explicit WeightPacker(Engine& en) : e(en) {}
+  // Register the matrix at `off`; reserves its per-row scale array (used by wo8).
+  void mat(size_t off, int rows, int cols, __half** w16, int8_t** w8, float** ws) {
+    const size_t so = reserve((size_t)rows * 4);
+    place(ws, so);
+    mats.push_back({off, so, rows, cols, w16, w8});
+  }
+  // Weight-only int8 (the reference's wo8 scheme, tools/quantize_wo8.py:42-46 via
+  // ai-edge-quantizer weight_only_wi8_afp32): per output row, symmetric, narrow range,
+  // scale = fp16(max|w| / 127), q = clamp(round_half_even(w / scale), -127, 127).
+  // The int8 row is written over the start of the matrix's own fp16 region.
+  void quantize_wo8() {
+    std::vector<float> row;
+    for (const Mat& m : mats) {
+      uint16_t* src = reinterpret_cast<uint16_t*>(staging.data() + m.off);
+      int8_t* dst = reinterpret_cast<int8_t*>(staging.data() + m.off);
+      float* sc = reinterpret_cast<float*>(staging.data() + m.scale_off);
+      row.resize(m.cols);
+      for (int r = 0; r < m.rows; ++r) {
+        float mx = 0.f;
+        for (int c = 0; c < m.cols; ++c) {
+          row[c] = h2f(src[(size_t)r * m.cols + c]);
+          mx = std::max(mx, std::fabs(row[c]));
+        }
+        float s16 = __half2float(__float2half_rn(mx / 127.f));
+        if (s16 == 0.f) s16 = 1.f;
+        sc[r] = s16;
+        for (int c = 0; c < m.cols; ++c) {
+          float q = std::nearbyint(row[c] / s16);
+          q = std::min(127.f, std::max(-127.f, q));
+          dst[(size_t)r * m.cols + c] = static_cast<int8_t>(q);
+        }
+      }
+    }
+  }
 
   const HostWeight* get(const std::string& k, size_t numel) {
     auto it = e.host.find(k);
@@ -227,6 +274,7 @@ struct WeightPacker {
     L.N = out; L.K = in;
     size_t o = reserve((size_t)in * out * 2);
     place(&L.w, o);
+    mat(o, out, in, &L.w, &L.w8, &L.ws);
     linear_rows(o, 0, in, pf + ".weight", in, out);
     if (bias) vecf(&L.b, pf + ".bias", out);
   }
@@ -235,6 +283,7 @@ struct WeightPacker {
     c.Co = co; c.Ci = ci; c.k = k;
     size_t o = reserve((size_t)co * ci * k * k * 2);
     place(&c.w, o);
+    mat(o, co, ci * k * k, &c.w, &c.w8, &c.ws);
     const HostWeight* hw = get(pf + ".weight", (size_t)co * ci * k * k);
     uint16_t* d = reinterpret_cast<uint16_t*>(staging.data() + o);
     for (int oc = 0; oc < co; ++oc)
@@ -246,9 +295,13 @@ struct WeightPacker {
   void conv1x1_as_linear(Lin& L, const std::string& pf, int ci, int co) {
     ConvW c;
     conv(c, pf, ci, co, 1);
-    // the fixups recorded pointers into c; re-target them at L
-    fixups[fixups.size() - 2].second = reinterpret_cast<void**>(&L.w);
+    // the fixups and matrix record point into c; re-target them at L
+    // (order of placements in conv(): w, scale, bias)
+    fixups[fixups.size() - 3].second = reinterpret_cast<void**>(&L.w);
+    fixups[fixups.size() - 2].second = reinterpret_cast<void**>(&L.ws);
     fixups[fixups.size() - 1].second = reinterpret_cast<void**>(&L.b);
+    mats.back().w16 = &L.w;
+    mats.back().w8 = &L.w8;
     L.N = co; L.K = ci;
   }
 };
@@ -266,6 +319,7 @@ int Engine::prepare() {
     w.conv_in.Co = 320; w.conv_in.Ci = 4; w.conv_in.k = 3;
     size_t o = P.reserve(320 * 64 * 2);
     P.place(&w.conv_in.w, o);
+    P.mat(o, 320, 64, &w.conv_in.w, &w.conv_in.w8, &w.conv_in.ws);
     const HostWeight* hw = P.get("conv_in.weight", 320 * 4 * 9);
     uint16_t* d = reinterpret_cast<uint16_t*>(P.staging.data() + o);
     for (int oc = 0; oc < 320; ++oc)
@@ -300,6 +354,7 @@ int Engine::prepare() {
       t.qkv.N = 3 * C; t.qkv.K = C;
       size_t o = P.reserve((size_t)3 * C * C * 2);
       P.place(&t.qkv.w, o);
+      P.mat(o, 3 * C, C, &t.qkv.w, &t.qkv.w8, &t.qkv.ws);
       P.linear_rows(o, 0, C, b + ".attn1.to_q.weight", C, C);
       P.linear_rows(o, C, C, b + ".attn1.to_k.weight", C, C);
       P.linear_rows(o, 2 * C, C, b + ".attn1.to_v.weight", C, C);
@@ -310,6 +365,7 @@ int Engine::prepare() {
       t.kv2.N = 2 * C; t.kv2.K = kCtxDim;
       size_t o = P.reserve((size_t)2 * C * kCtxDim * 2);
       P.place(&t.kv2.w, o);
+      P.mat(o, 2 * C, kCtxDim, &t.kv2.w, &t.kv2.w8, &t.kv2.ws);
       P.linear_rows(o, 0, kCtxDim, b + ".attn2.to_k.weight", kCtxDim, C);
       P.linear_rows(o, C, kCtxDim, b + ".attn2.to_v.weight", kCtxDim, C);
     }
@@ -317,10 +373,11 @@ int Engine::prepare() {
     {  // GEGLU proj [8C][C] re-tiled: each 256-row tile = [128 value rows ; 128 gate rows]
       const int N = 8 * C, half = 4 * C;
       t.ff1.N = N; t.ff1.K = C;
-      size_t tmp = P.reserve((size_t)N * C * 2);
+      size_t tmp = P.reserve((size_t)N * C * 2);  // unreordered copy (host staging only)
       P.linear_rows(tmp, 0, C, b + ".ff.net.0.proj.weight", C, N);
       size_t o = P.reserve((size_t)N * C * 2);
       P.place(&t.ff1.w, o);
+      P.mat(o, N, C, &t.ff1.w, &t.ff1.w8, &t.ff1.ws);
       size_t bo = P.reserve((size_t)N * 4);
       P.place(&t.ff1.b, bo);
       const HostWeight* hb = P.get(b + ".ff.net.0.proj.bias", N);
@@ -389,6 +446,7 @@ int Engine::prepare() {
     w.tp_N = total;
     size_t o = P.reserve((size_t)total * kTemb * 2);
     P.place(&w.tp_w, o);
+    P.mat(o, total, kTemb, &w.tp_w, &w.tp_w8, &w.tp_ws);
     size_t bo = P.reserve((size_t)total * 4);
     P.place(&w.tp_b, bo);
     float* bd = reinterpret_cast<float*>(P.staging.data() + bo);
@@ -399,17 +457,34 @@ int Engine::prepare() {
     }
   }
   if (!P.missing.empty()) return fail(SDG_ERR_MISSING_WEIGHT, "weight " + P.missing);
+  if (wo8) P.quantize_wo8();
   SDG_CUDA_TRY(cudaSetDevice(device));
   SDG_CUDA_TRY(cudaMalloc(&warena, P.off));
   warena_bytes = P.off;
   SDG_CUDA_TRY(cudaMemcpy(warena, P.staging.data(), P.off, cudaMemcpyHostToDevice));
   for (auto& f : P.fixups) *f.second = warena + f.first;
+  for (auto& m : P.mats) {
+    if (wo8) {
+      *m.w8 = reinterpret_cast<int8_t*>(warena + m.off);
+      *m.w16 = nullptr;
+    } else {
+      *m.w8 = nullptr;
+    }
+  }
   host.clear();
   prepared = true;
   return SDG_OK;
 }
 
 // ------------------------------------------------------------------ builder ops
+static inline void set_w(GemmArgs& a, const __half* w, const int8_t* w8, const float* ws) {
+  if (w8) {
+    a.w = nullptr; a.w8 = w8; a.wscale = ws;
+  } else {
+    a.w = w;
+  }
+}
+
 void Builder::begin_op(int cat) {
   (void)cat;
   if (profile && !dry_) {
@@ -485,7 +560,7 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
     GemmArgs a;
     a.M = M; a.N = r.cout; a.K = 9 * r.cin; a.taps = 9;
     a.a0 = h; a.cin0 = r.cin; a.B = B; a.H = H; a.W = W;
-    a.w = r.c1.w; a.bias = r.c1.b;
+    set_w(a, r.c1.w, r.c1.w8, r.c1.ws); a.bias = r.c1.b;
     a.rowbias = tp_all_ ? tp_all_ + r.tp_off : nullptr; a.rowbias_ld = e_.w.tp_N; a.rows_per_image = HW;
     a.out = h2;
     gemm(a, kCatConv3);
@@ -499,7 +574,7 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
     a.M = M; a.N = r.cout; a.K = x.C + (x2 ? x2->C : 0); a.taps = 1;
     a.a0 = x.p; a.cin0 = x.C;
     if (x2) { a.a1 = x2->p; a.cin1 = x2->C; }
-    a.w = r.sc.w; a.bias = r.sc.b; a.out = sc;
+    set_w(a, r.sc.w, r.sc.w8, r.sc.ws); a.bias = r.sc.b; a.out = sc;
     gemm(a, kCatGemm);
     resid = sc;
   }
@@ -507,7 +582,7 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
     GemmArgs a;
     a.M = M; a.N = r.cout; a.K = 9 * r.cout; a.taps = 9;
     a.a0 = h3; a.cin0 = r.cout; a.B = B; a.H = H; a.W = W;
-    a.w = r.c2.w; a.bias = r.c2.b; a.residual = resid; a.out = out.p;
+    set_w(a, r.c2.w, r.c2.w8, r.c2.ws); a.bias = r.c2.b; a.residual = resid; a.out = out.p;
     gemm(a, kCatConv3);
   }
   off_ = mark;
@@ -529,7 +604,8 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   __half* gg = alloc_h((size_t)M * 4 * C);
   auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
     GemmArgs a;
-    a.M = M; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; a.w = L.w; a.bias = L.b; a.residual = resid; a.out = y;
+    a.M = M; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b; a.residual = resid;
+    a.out = y;
     gemm(a, kCatGemm);
   };
   auto ln = [&](const __half* xin, const Norm& n) {
@@ -541,7 +617,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
                    int vt_idx, int spad) {
     GemmArgs a;
-    a.M = Mr; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; a.w = L.w; a.bias = L.b;
+    a.M = Mr; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b;
     a.epi = kEpiHeads; a.rows_per_image = rows_per_image;
     a.head_out[0] = o0; a.head_out[1] = o1; a.head_out[2] = o2;
     a.head_C = C; a.heads = kHeads; a.head_d = d; a.head_dp = dp;
@@ -571,7 +647,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   ln(tt, t.ln3);
   {
     GemmArgs a;
-    a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = hn; a.cin0 = C; a.w = t.ff1.w; a.bias = t.ff1.b;
+    a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = hn; a.cin0 = C; set_w(a, t.ff1.w, t.ff1.w8, t.ff1.ws); a.bias = t.ff1.b;
     a.epi = kEpiGeglu; a.out = gg; a.ld_out = 4 * C;
     gemm(a, kCatGemm);
   }
@@ -593,7 +669,8 @@ Buf Builder::downsample(const ConvW& c, const Buf& x, int H, int W) {
     launches_++;
   }
   GemmArgs a;
-  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.a0 = col; a.cin0 = 9 * x.C; a.w = c.w; a.bias = c.b; a.out = out.p;
+  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.a0 = col; a.cin0 = 9 * x.C; set_w(a, c.w, c.w8, c.ws); a.bias = c.b;
+  a.out = out.p;
   gemm(a, kCatGemm);
   off_ = mark;
   return out;
@@ -612,7 +689,7 @@ Buf Builder::upsample(const ConvW& c, const Buf& x, int H, int W) {
   }
   GemmArgs a;
   a.M = M; a.N = c.Co; a.K = 9 * x.C; a.taps = 9; a.a0 = up; a.cin0 = x.C; a.B = B; a.H = Ho; a.W = Wo;
-  a.w = c.w; a.bias = c.b; a.out = out.p;
+  set_w(a, c.w, c.w8, c.ws); a.bias = c.b; a.out = out.p;
   gemm(a, kCatConv3);
   off_ = mark;
   return out;
@@ -651,11 +728,14 @@ int Builder::run() {
     begin_op(kCatMisc);
     check(launch_time_embedding(pl_.t_in, B, B, pl_.mode == 1 ? pl_.tproj_in : nullptr, te, s_), "time_embedding", kCatMisc);
     begin_op(kCatGemv);
-    check(launch_gemv(te, B, 320, w.t1.w, w.t1.b, kTemb, 0, 1, t1, kTemb, s_), "time mlp 1", kCatGemv, (B + 7) / 8);
+    check(launch_gemv(te, B, 320, w.t1.w, w.t1.w8, w.t1.ws, w.t1.b, kTemb, 0, 1, t1, kTemb, s_), "time mlp 1",
+          kCatGemv, (B + 7) / 8);
     begin_op(kCatGemv);
-    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.b, kTemb, 0, 0, temb, kTemb, s_), "time mlp 2", kCatGemv, (B + 7) / 8);
+    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.w8, w.t2.ws, w.t2.b, kTemb, 0, 0, temb, kTemb, s_), "time mlp 2",
+          kCatGemv, (B + 7) / 8);
     begin_op(kCatGemv);
-    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_b, w.tp_N, 1, 0, tp_all_, w.tp_N, s_), "time_emb_proj", kCatGemv, (B + 7) / 8);
+    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_w8, w.tp_ws, w.tp_b, w.tp_N, 1, 0, tp_all_, w.tp_N, s_),
+          "time_emb_proj", kCatGemv, (B + 7) / 8);
     begin_op(kCatMisc);
     check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
   } else {
@@ -673,7 +753,8 @@ int Builder::run() {
       launches_++;
     }
     GemmArgs a;
-    a.M = M; a.N = 320; a.K = 64; a.a0 = col; a.cin0 = 64; a.w = w.conv_in.w; a.bias = w.conv_in.b; a.out = x.p;
+    a.M = M; a.N = 320; a.K = 64; a.a0 = col; a.cin0 = 64; set_w(a, w.conv_in.w, w.conv_in.w8, w.conv_in.ws);
+    a.bias = w.conv_in.b; a.out = x.p;
     gemm(a, kCatGemm);
     off_ = mark;
   }
@@ -712,7 +793,8 @@ int Builder::run() {
     gn(x, nullptr, B, HW, w.norm_out, kResEps, true, g);
     GemmArgs a;
     a.M = M; a.N = 4; a.K = 9 * 320; a.taps = 9; a.a0 = g; a.cin0 = 320; a.B = B; a.H = H; a.W = W;
-    a.w = w.conv_out.w; a.bias = w.conv_out.b; a.epi = kEpiNchwF32; a.out_f32 = pl_.out; a.rows_per_image = HW;
+    set_w(a, w.conv_out.w, w.conv_out.w8, w.conv_out.ws); a.bias = w.conv_out.b; a.epi = kEpiNchwF32;
+    a.out_f32 = pl_.out; a.rows_per_image = HW;
     gemm(a, kCatConv3);
     off_ = mark;
   }
@@ -898,6 +980,13 @@ SDG_API int sdg_load_dir(sdg_engine* h, const char* dir) {
   if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
   if (!dir) return fail(SDG_ERR_ARG, "dir is null");
   return sdg_internal_load_dir(h, dir);
+}
+
+SDG_API int sdg_quantize_wo8(sdg_engine* h) {
+  if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
+  if (h->e.prepared) return fail(SDG_ERR_ARG, "sdg_quantize_wo8 must come before the first forward / sdg_prepare");
+  h->e.wo8 = true;
+  return SDG_OK;
 }
 
 SDG_API int sdg_prepare(sdg_engine* h) {

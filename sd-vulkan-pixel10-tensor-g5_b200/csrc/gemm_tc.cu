@@ -10,6 +10,11 @@
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps
 // the main loop of tile i+1. No cluster multicast is used anywhere.
 //
+// Weight-only int8 (wo8): W arrives as int8 by TMA into a staging tile;
+// 4 converter warps (warps 6..9) rewrite it as fp16 (exact) in the swizzled
+// B layout while the MMA runs, and the per-output-channel scale is applied in
+// the epilogue (sum_k a*(q*s) = s * sum_k a*q).
+//
 // Split-K: when M is small (deep UNet levels) the K range is divided among
 // CTAs; each writes fp32 partials to a workspace and a reduce kernel sums the
 // splits in a fixed order and applies the same fused epilogue, so results are
@@ -28,7 +33,6 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
 constexpr uint32_t kATileBytes = BM * BK * 2;  // 16 KB
 
 struct GemmDev {
@@ -52,19 +56,23 @@ struct GemmDev {
   int head_vt, head_d16, head_spad;
   int splits, kb_per_split;  // split-K
   float* ws;                 // [splits][M][N] fp32 partials when splits > 1
+  const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
 };
 
-template <int BN>
+template <int BN, bool W8>
 struct Cfg {
+  static constexpr int kThreads = W8 ? 320 : 192;
   static constexpr uint32_t kBTileBytes = BN * BK * 2;
-  static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr uint32_t kB8Bytes = W8 ? BN * BK : 0;  // int8 staging tile
+  static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes + kB8Bytes;
+  static constexpr uint32_t kTxBytes = kATileBytes + (W8 ? kB8Bytes : kBTileBytes);  // bytes TMA delivers per stage
   // as many stages as shared memory holds: TMA latency from L2 needs deep pipelines
-  static constexpr int kStages = (232448 - 1024 - 256) / kStageBytes > 12 ? 12 : (232448 - 1024 - 256) / kStageBytes;
+  static constexpr int kStages = (232448 - 1024 - 512) / kStageBytes > 12 ? 12 : (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kAccStride = BN <= 16 ? 16 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
   static constexpr uint32_t kTmemCols = (2 * kAccStride) < 32 ? 32 : 2 * kAccStride;
   static constexpr int kChunk = BN >= 32 ? 32 : 16;
-  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 512;  // tail: barriers + TMEM slot
   static_assert(kSmem <= 232448, "GEMM tile configuration exceeds 227 KB of shared memory");
 };
 
@@ -92,6 +100,10 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
 // Not used for GEGLU (which pairs two column ranges).
 __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int n, float (&v)[8]) {
   const int img = m / p.rows_per_image;
+  if (p.wscale) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + min(n + j, p.N - 1));
+  }
   if (p.epi == kEpiNchwF32) {
     const int pix = m - img * p.rows_per_image;
 #pragma unroll
@@ -140,19 +152,33 @@ __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int n, float 
   *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + n) = pack8(v);
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+// int8 x4 (one 32-bit word) -> two fp16x2, exact: bias the bytes to unsigned,
+// splice each under the fp16 exponent of 1024 (0x64), subtract 1024 + 128.
+__device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  uint32_t a = __byte_perm(x, 0x64646464u, 0x4140);
+  uint32_t b = __byte_perm(x, 0x64646464u, 0x4342);
+  const __half2 k = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152.0
+  __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), k);
+  __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), k);
+  lo = *reinterpret_cast<uint32_t*>(&ha);
+  hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+template <int BN, bool W8>
+__global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_w, const GemmDev p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, W8>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kATileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * C::kBTileBytes);
-  // bars: full[S], empty[S], tfull[2], tempty[2], drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint8_t* sB8 = sB + S * C::kBTileBytes;  // int8 staging (wo8 only)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB8 + S * C::kB8Bytes);
+  // bars: full[S], empty[S], tfull[2], tempty[2], drain, conv[S] (wo8: fp16 B tile ready)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -162,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * S + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * S + 2 + a); };
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
+  auto conv_bar = [&](int s) { return bar0 + 8u * (2 * S + 5 + s); };
 
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
@@ -189,6 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty_bar(a), 4);
     }
     mbar_init(drain_bar, 1);
+    if constexpr (W8)
+      for (int s = 0; s < S; ++s) mbar_init(conv_bar(s), 128);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -227,11 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(full_bar(s), C::kStageBytes);
+          mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
           issued[s] = true;
           last_phase[s] = ph;
           const uint32_t dA = smem_u32(sA + s * kATileBytes);
-          const uint32_t dB = smem_u32(sB + s * C::kBTileBytes);
+          const uint32_t dB = W8 ? smem_u32(sB8 + s * C::kB8Bytes) : smem_u32(sB + s * C::kBTileBytes);
           const int tap = kb / kb_per_tap;
           const int cc = (kb % kb_per_tap) * BK;
           const bool second = cc >= p.cin0;
@@ -269,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+          if (W8 && !mbar_wait(conv_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
           const uint64_t da = sdesc_sw128(smem_u32(sA + s * kATileBytes), 16, 1024);
           const uint64_t db = sdesc_sw128(smem_u32(sB + s * C::kBTileBytes), 16, 1024);
@@ -283,6 +313,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every issued MMA has retired before TMEM is released
       mma_commit(drain_bar);
       mbar_wait(drain_bar, 0, p.err, kDevTimeoutDrain);
+    }
+  } else if (W8 && warp >= 6) {
+    // ------------------------------------------------------------ int8 -> fp16 converters (wo8)
+    const int ct = threadIdx.x - 192;  // 0..127
+    uint32_t it = 0;
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      int m_blk, n_blk, kb0, kb1;
+      decode(unit, m_blk, n_blk, kb0, kb1);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1u;
+        ok = mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull);
+        if (!ok) break;
+        const uint8_t* src = sB8 + s * C::kB8Bytes;
+        uint8_t* dst = sB + s * C::kBTileBytes;
+#pragma unroll 2
+        for (int i = ct; i < BN * 4; i += 128) {  // 16 int8 of row i/4 -> two 16-byte fp16 chunks
+          const int row = i >> 2, c = i & 3;
+          const uint4 q = *reinterpret_cast<const uint4*>(src + row * 64 + c * 16);
+          uint4 h0, h1;
+          i8x4_to_h4(q.x, h0.x, h0.y);
+          i8x4_to_h4(q.y, h0.z, h0.w);
+          i8x4_to_h4(q.z, h1.x, h1.y);
+          i8x4_to_h4(q.w, h1.z, h1.w);
+          const int r7 = row & 7;
+          *reinterpret_cast<uint4*>(dst + row * 128 + (((2 * c) ^ r7) << 4)) = h0;
+          *reinterpret_cast<uint4*>(dst + row * 128 + (((2 * c + 1) ^ r7) << 4)) = h1;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(conv_bar(s));
+      }
+      if (!ok) break;
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -326,8 +389,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 const int cj = c + g * 8 + j;
-                const float a = __uint_as_float(ra[g * 8 + j]) + (p.bias ? __ldg(p.bias + n0 + cj) : 0.f);
-                const float gt = __uint_as_float(rg[g * 8 + j]) + (p.bias ? __ldg(p.bias + n0 + HALF + cj) : 0.f);
+                float a = __uint_as_float(ra[g * 8 + j]), gt = __uint_as_float(rg[g * 8 + j]);
+                if (p.wscale) {
+                  a *= __ldg(p.wscale + n0 + cj);
+                  gt *= __ldg(p.wscale + n0 + HALF + cj);
+                }
+                a += p.bias ? __ldg(p.bias + n0 + cj) : 0.f;
+                gt += p.bias ? __ldg(p.bias + n0 + HALF + cj) : 0.f;
                 v[j] = a * gelu_erf(gt);
               }
               *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc + g * 8) = pack8(v);
@@ -408,21 +476,22 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
   }
 }
 
-template <int BN>
+template <int BN, bool W8>
 cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1, const CUtensorMap& mw,
                       cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, W8>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const int units = ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.splits;
   const int grid = std::max(1, std::min(units, num_sms()));
-  gemm_tc_kernel<BN><<<grid, kThreads, C::kSmem, s>>>(ma0, ma1, mw, d);
+  gemm_tc_kernel<BN, W8><<<grid, C::kThreads, C::kSmem, s>>>(ma0, ma1, mw, d);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || d.splits == 1) return e;
   const size_t total = (size_t)d.M * ((d.N + 7) / 8);
@@ -500,7 +569,7 @@ int gemm_launch_count(const GemmArgs& a) {
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   const int cin = a.cin0 + a.cin1;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK != 0 || cin % BK != 0 || a.cin0 % BK != 0 ||
-      a.K != a.taps * cin || !(a.taps == 1 || a.taps == 9) || a.w == nullptr || a.a0 == nullptr ||
+      a.K != a.taps * cin || !(a.taps == 1 || a.taps == 9) || (a.w == nullptr && a.w8 == nullptr) || a.a0 == nullptr ||
       (a.cin1 > 0 && a.a1 == nullptr))
     return cudaErrorInvalidValue;
   if (a.epi != kEpiNchwF32 && a.epi != kEpiGeglu && a.N % 16 != 0) return cudaErrorInvalidValue;
@@ -530,7 +599,9 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.head_C = a.head_C; d.heads = a.heads; d.head_d = a.head_d; d.head_dp = a.head_dp;
   d.head_vt = a.head_vt; d.head_d16 = a.head_d16; d.head_spad = a.head_spad;
   d.splits = tc.splits; d.kb_per_split = tc.kb_per_split; d.ws = a.ws;
+  d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
+  if (a.w8 && !a.wscale) return cudaErrorInvalidValue;
 
   CUtensorMap ma0{}, ma1{}, mw{};
   if (a.taps == 9) {
@@ -562,14 +633,30 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
     }
   }
   if (a.cin1 == 0) ma1 = ma0;
+  if (a.w8) {
+    // int8 weights: 64-byte rows of [N, K], no swizzle (the converters re-lay them out)
+    uint64_t dims[2] = {(uint64_t)a.K, (uint64_t)a.N};
+    uint64_t str[1] = {(uint64_t)a.K};
+    uint32_t box[2] = {BK, (uint32_t)bn};
+    if (!make_tmap(&mw, a.w8, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_DATA_TYPE_UINT8))
+      return cudaErrorInvalidValue;
+    switch (bn) {
+      case 16: return launch_bn<16, true>(d, ma0, ma1, mw, s);
+      case 64: return launch_bn<64, true>(d, ma0, ma1, mw, s);
+      case 128: return launch_bn<128, true>(d, ma0, ma1, mw, s);
+      case 160: return launch_bn<160, true>(d, ma0, ma1, mw, s);
+      case 256: return launch_bn<256, true>(d, ma0, ma1, mw, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (!make_tmap_2d(&mw, a.w, a.N, a.K, a.K, bn, BK)) return cudaErrorInvalidValue;
 
   switch (bn) {
-    case 16: return launch_bn<16>(d, ma0, ma1, mw, s);
-    case 64: return launch_bn<64>(d, ma0, ma1, mw, s);
-    case 128: return launch_bn<128>(d, ma0, ma1, mw, s);
-    case 160: return launch_bn<160>(d, ma0, ma1, mw, s);
-    case 256: return launch_bn<256>(d, ma0, ma1, mw, s);
+    case 16: return launch_bn<16, false>(d, ma0, ma1, mw, s);
+    case 64: return launch_bn<64, false>(d, ma0, ma1, mw, s);
+    case 128: return launch_bn<128, false>(d, ma0, ma1, mw, s);
+    case 160: return launch_bn<160, false>(d, ma0, ma1, mw, s);
+    case 256: return launch_bn<256, false>(d, ma0, ma1, mw, s);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -34,7 +34,10 @@ __global__ void time_embedding_kernel(const float* t, int n_t, int B, const floa
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvMaxK = 1280;
 
+// One warp per output n; W8 = weight-only int8 rows [N, K] with per-row scale ws[n].
+template <bool W8>
 __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, int M, int K, const __half* __restrict__ w,
+                                                   const int8_t* __restrict__ w8, const float* __restrict__ ws,
                                                    const float* __restrict__ bias, int N, int act_in, int act_out,
                                                    float* __restrict__ y, int ldy) {
   __shared__ float xs[kGemvMaxM * kGemvMaxK];
@@ -46,19 +49,25 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * (blockDim.x >> 5) + warp;
   if (n >= N) return;
-  const __half* wr = w + (size_t)n * K;
   float acc[kGemvMaxM];
 #pragma unroll
   for (int m = 0; m < kGemvMaxM; ++m) acc[m] = 0.f;
   for (int k0 = lane * 8; k0 < K; k0 += 256) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(wr + k0));
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
     float wf[8];
+    if constexpr (W8) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(w8 + (size_t)n * K + k0));
+      const uint32_t b4[2] = {u.x, u.y};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float2 f = __half22float2(h[e]);
-      wf[2 * e] = f.x;
-      wf[2 * e + 1] = f.y;
+      for (int e = 0; e < 8; ++e) wf[e] = (float)(int8_t)((b4[e >> 2] >> (8 * (e & 3))) & 0xff);
+    } else {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(w + (size_t)n * K + k0));
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __half22float2(h[e]);
+        wf[2 * e] = f.x;
+        wf[2 * e + 1] = f.y;
+      }
     }
 #pragma unroll
     for (int m = 0; m < kGemvMaxM; ++m) {
@@ -74,6 +83,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
     float v = acc[m];
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (lane == 0 && m < M) {
+      if constexpr (W8) v *= ws[n];
       v += bias ? bias[n] : 0.f;
       if (act_out) v = silu_f(v);
       y[(size_t)m * ldy + n] = v;
@@ -196,13 +206,19 @@ cudaError_t launch_time_embedding(const float* t, int n_t, int B, const float* t
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const float* bias, int N, int act_in, int act_out,
-                        float* y, int ldy, cudaStream_t s) {
+cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int8_t* w8, const float* ws,
+                        const float* bias, int N, int act_in, int act_out, float* y, int ldy, cudaStream_t s) {
   if (M <= 0 || K <= 0 || K > kGemvMaxK || K % 8) return cudaErrorInvalidValue;
+  if ((w8 != nullptr) == (w != nullptr) || (w8 && !ws)) return cudaErrorInvalidValue;
   const int blocks = (N + 7) / 8;
   for (int m0 = 0; m0 < M; m0 += kGemvMaxM) {  // rows in chunks of kGemvMaxM
     const int mc = M - m0 < kGemvMaxM ? M - m0 : kGemvMaxM;
-    gemv_kernel<<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, w, bias, N, act_in, act_out, y + (size_t)m0 * ldy, ldy);
+    if (w8)
+      gemv_kernel<true><<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, nullptr, w8, ws, bias, N, act_in, act_out,
+                                               y + (size_t)m0 * ldy, ldy);
+    else
+      gemv_kernel<false><<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, w, nullptr, nullptr, bias, N, act_in,
+                                                act_out, y + (size_t)m0 * ldy, ldy);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

@@ -31,6 +31,8 @@ struct GemmArgs {
   int lda0 = 0, lda1 = 0;      // row strides (elements) for taps == 1 (default cin)
   int B = 1, H = 1, W = 1;     // conv geometry (taps == 9)
   const __half* w = nullptr;   // [N, K] K-major (conv: [Co][tap][Cin])
+  const int8_t* w8 = nullptr;  // weight-only int8 alternative to w: [N, K] ...
+  const float* wscale = nullptr;  // ... with per-row (output channel) scale [N]
   // epilogue
   int epi = kEpiPlain;
   int act = 0;                      // 0 none, 1 SiLU
@@ -91,9 +93,10 @@ cudaError_t launch_attention(const AttnArgs& a, int* dev_err, cudaStream_t s);
 // small kernels (sdg_misc.cu)
 cudaError_t launch_time_embedding(const float* timesteps, int n_t, int B, const float* temb_proj_in, float* out320,
                                   cudaStream_t s);
-// y[m, n] = act(x[m,:] . w[n,:] + bias[n]) for small M (<= 8); x fp32 [M,K], w fp16 [N,K], y fp32.
-cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const float* bias, int N, int act_in,
-                        int act_out, float* y, int ldy, cudaStream_t s);
+// y[m, n] = act(x[m,:] . w[n,:] + bias[n]) for small M; x fp32 [M,K], y fp32. Weights are
+// either fp16 w [N,K], or int8 w8 [N,K] with per-row scale ws [N] (exactly one of w / w8).
+cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int8_t* w8, const float* ws,
+                        const float* bias, int N, int act_in, int act_out, float* y, int ldy, cudaStream_t s);
 cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int stride, int Kpad, __half* col,
                              cudaStream_t s);
 cudaError_t launch_latent_im2col(const float* lat_nchw, int B, int C, int H, int W, int Kpad, __half* col,
