@@ -22,6 +22,7 @@
 #include <algorithm>
 
 #include "sdg_kernels.h"
+#include "sdg_launch.h"
 #include "sdg_ptx.cuh"
 #include "sdg_tma.h"
 
@@ -128,6 +129,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (Q/K/V) are visible from here on
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -405,8 +408,7 @@ cudaError_t launch_cfg(const AttnArgs& a, int* err, cudaStream_t s) {
     return cudaErrorInvalidValue;
   AttnDev d{a.heads, a.Sq, a.Sk, a.d, a.o, a.ld_o, a.scale * 1.4426950408889634f, err};
   dim3 grid((a.Sq + 128 * CF::NQT - 1) / (128 * CF::NQT), a.BH);
-  attn_tc_kernel<CF><<<grid, CF::kThreads, CF::kSmem, s>>>(mq, mk, mv, d);
-  return cudaGetLastError();
+  return launch_kernel(attn_tc_kernel<CF>, grid, dim3(CF::kThreads), CF::kSmem, s, 0, mq, mk, mv, d);
 }
 
 }  // namespace

@@ -24,6 +24,7 @@
 #include <cstdio>
 
 #include "sdg_kernels.h"
+#include "sdg_launch.h"
 #include "sdg_ptx.cuh"
 #include "sdg_tma.h"
 
@@ -233,6 +234,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are visible from here on
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -454,6 +457,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
 // Sum split-K partials in split order and apply the fused epilogue; one
 // thread per 8 output columns.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
+  pdl_wait();
+  pdl_trigger();
   const int ngrp = (p.N + 7) / 8;
   const size_t total = (size_t)p.M * ngrp;
   const size_t plane = (size_t)p.M * p.N;
@@ -491,13 +496,11 @@ cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMa
   }
   const int units = ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.splits;
   const int grid = std::max(1, std::min(units, num_sms()));
-  gemm_tc_kernel<BN, W8><<<grid, C::kThreads, C::kSmem, s>>>(ma0, ma1, mw, d);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(gemm_tc_kernel<BN, W8>, dim3(grid), dim3(C::kThreads), C::kSmem, s, 0, ma0, ma1, mw, d);
   if (e != cudaSuccess || d.splits == 1) return e;
   const size_t total = (size_t)d.M * ((d.N + 7) / 8);
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
-  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(d);
-  return cudaGetLastError();
+  return launch_kernel(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, s, 0, d);
 }
 
 struct TileChoice {

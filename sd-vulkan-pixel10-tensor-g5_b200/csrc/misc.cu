@@ -8,12 +8,15 @@
 #include <cmath>
 
 #include "sdg_kernels.h"
+#include "sdg_launch.h"
 #include "sdg_ptx.cuh"
 
 namespace sdg {
 namespace {
 
 __global__ void time_embedding_kernel(const float* t, int n_t, int B, const float* tin, float* out) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int i = threadIdx.x;  // 0..159
   if (i >= 160) return;
@@ -40,6 +43,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
                                                    const int8_t* __restrict__ w8, const float* __restrict__ ws,
                                                    const float* __restrict__ bias, int N, int act_in, int act_out,
                                                    float* __restrict__ y, int ldy) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float xs[kGemvMaxM * kGemvMaxK];
   for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
     const float v = x[i];
@@ -94,6 +99,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
 // col[(b*Ho+oy)*Wo+ox, tap*C + c] = x[b, oy*s+ky-1, ox*s+kx-1, c] (0 outside)
 __global__ void im2col3x3_kernel(const __half* __restrict__ x, int B, int H, int W, int C, int stride, int Ho, int Wo,
                                  int Kpad, __half* __restrict__ col) {
+  pdl_wait();
+  pdl_trigger();
   const int nvec = C / 8;
   const size_t total = (size_t)B * Ho * Wo * 9 * nvec;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -114,6 +121,8 @@ __global__ void im2col3x3_kernel(const __half* __restrict__ x, int B, int H, int
 // conv_in operand: lat NCHW fp32 [B,Cl,H,W] -> col [B*H*W, Kpad], K index = tap*Cl + c, zero padded.
 __global__ void latent_im2col_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W, int Kpad,
                                      __half* __restrict__ col) {
+  pdl_wait();
+  pdl_trigger();
   const size_t total = (size_t)B * H * W * Kpad;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int k = (int)(i % Kpad);
@@ -130,6 +139,8 @@ __global__ void latent_im2col_kernel(const float* __restrict__ lat, int B, int C
 }
 
 __global__ void upsample2x_kernel(const __half* __restrict__ x, int B, int H, int W, int C, __half* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const int nvec = C / 8;
   const int Ho = 2 * H, Wo = 2 * W;
   const size_t total = (size_t)B * Ho * Wo * nvec;
@@ -144,6 +155,8 @@ __global__ void upsample2x_kernel(const __half* __restrict__ x, int B, int H, in
 
 __global__ void concat_kernel(const __half* __restrict__ a, int Ca, const __half* __restrict__ b, int Cb, int rows,
                               __half* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const int C = Ca + Cb, nvec = C / 8;
   const size_t total = (size_t)rows * nvec;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -155,6 +168,8 @@ __global__ void concat_kernel(const __half* __restrict__ a, int Ca, const __half
 }
 
 __global__ void add_kernel(const __half2* __restrict__ a, const __half2* __restrict__ b, size_t n2, __half2* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n2; i += (size_t)gridDim.x * blockDim.x) {
     const float2 fa = __half22float2(a[i]), fb = __half22float2(b[i]);
     y[i] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
@@ -162,6 +177,8 @@ __global__ void add_kernel(const __half2* __restrict__ a, const __half2* __restr
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, size_t n, __half* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
     y[i] = __float2half_rn(x[i]);
 }
@@ -173,6 +190,8 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ x, size_t n, __half*
 __global__ void cfg_lcm_kernel(const float* __restrict__ eps2, float* __restrict__ lat, const float* __restrict__ noise,
                                int n_img, int L, float cfg, double c_skip, double c_out, double sa, double sb,
                                double sap, double sbp, int last, float* __restrict__ lat_pair) {
+  pdl_wait();
+  pdl_trigger();
   const size_t total = (size_t)n_img * L;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t img = i / L, j = i % L;
@@ -202,8 +221,7 @@ inline int grid_for(size_t n, int threads = 256) {
 
 cudaError_t launch_time_embedding(const float* t, int n_t, int B, const float* tin, float* out320, cudaStream_t s) {
   if (B <= 0 || (n_t != 1 && n_t != B)) return cudaErrorInvalidValue;
-  time_embedding_kernel<<<B, 160, 0, s>>>(t, n_t, B, tin, out320);
-  return cudaGetLastError();
+  return launch_kernel(time_embedding_kernel, dim3(B), dim3(160), 0, s, 0, t, n_t, B, tin, out320);
 }
 
 cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int8_t* w8, const float* ws,
@@ -213,13 +231,14 @@ cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int
   const int blocks = (N + 7) / 8;
   for (int m0 = 0; m0 < M; m0 += kGemvMaxM) {  // rows in chunks of kGemvMaxM
     const int mc = M - m0 < kGemvMaxM ? M - m0 : kGemvMaxM;
+    cudaError_t e;
     if (w8)
-      gemv_kernel<true><<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, nullptr, w8, ws, bias, N, act_in, act_out,
-                                               y + (size_t)m0 * ldy, ldy);
+      e = launch_kernel(gemv_kernel<true>, dim3(blocks), dim3(256), 0, s, 0, x + (size_t)m0 * K, mc, K,
+                        (const __half*)nullptr, w8, ws, bias, N, act_in, act_out, y + (size_t)m0 * ldy, ldy);
     else
-      gemv_kernel<false><<<blocks, 256, 0, s>>>(x + (size_t)m0 * K, mc, K, w, nullptr, nullptr, bias, N, act_in,
-                                                act_out, y + (size_t)m0 * ldy, ldy);
-    cudaError_t e = cudaGetLastError();
+      e = launch_kernel(gemv_kernel<false>, dim3(blocks), dim3(256), 0, s, 0, x + (size_t)m0 * K, mc, K, w,
+                        (const int8_t*)nullptr, (const float*)nullptr, bias, N, act_in, act_out,
+                        y + (size_t)m0 * ldy, ldy);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -230,50 +249,44 @@ cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int st
   if (C % 8 || Kpad < 9 * C) return cudaErrorInvalidValue;
   const int Ho = (H + 2 - 3) / stride + 1, Wo = (W + 2 - 3) / stride + 1;
   const size_t total = (size_t)B * Ho * Wo * 9 * (C / 8);
-  im2col3x3_kernel<<<grid_for(total), 256, 0, s>>>(x, B, H, W, C, stride, Ho, Wo, Kpad, col);
-  return cudaGetLastError();
+  return launch_kernel(im2col3x3_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, x, B, H, W, C, stride, Ho, Wo, Kpad,
+                       col);
 }
 
 cudaError_t launch_latent_im2col(const float* lat, int B, int Cl, int H, int W, int Kpad, __half* col, cudaStream_t s) {
   if (Kpad < 9 * Cl) return cudaErrorInvalidValue;
   const size_t total = (size_t)B * H * W * Kpad;
-  latent_im2col_kernel<<<grid_for(total), 256, 0, s>>>(lat, B, Cl, H, W, Kpad, col);
-  return cudaGetLastError();
+  return launch_kernel(latent_im2col_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, lat, B, Cl, H, W, Kpad, col);
 }
 
 cudaError_t launch_upsample2x(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t s) {
   if (C % 8) return cudaErrorInvalidValue;
   const size_t total = (size_t)B * 4 * H * W * (C / 8);
-  upsample2x_kernel<<<grid_for(total), 256, 0, s>>>(x, B, H, W, C, y);
-  return cudaGetLastError();
+  return launch_kernel(upsample2x_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, x, B, H, W, C, y);
 }
 
 cudaError_t launch_concat(const __half* a, int Ca, const __half* b, int Cb, int rows, __half* y, cudaStream_t s) {
   if (Ca % 8 || Cb % 8) return cudaErrorInvalidValue;
   const size_t total = (size_t)rows * ((Ca + Cb) / 8);
-  concat_kernel<<<grid_for(total), 256, 0, s>>>(a, Ca, b, Cb, rows, y);
-  return cudaGetLastError();
+  return launch_kernel(concat_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, a, Ca, b, Cb, rows, y);
 }
 
 cudaError_t launch_add(const __half* a, const __half* b, size_t n, __half* y, cudaStream_t s) {
   if (n % 2) return cudaErrorInvalidValue;
-  add_kernel<<<grid_for(n / 2), 256, 0, s>>>(reinterpret_cast<const __half2*>(a), reinterpret_cast<const __half2*>(b), n / 2,
-                                             reinterpret_cast<__half2*>(y));
-  return cudaGetLastError();
+  return launch_kernel(add_kernel, dim3(grid_for(n / 2)), dim3(256), 0, s, 0, reinterpret_cast<const __half2*>(a),
+                       reinterpret_cast<const __half2*>(b), n / 2, reinterpret_cast<__half2*>(y));
 }
 
 cudaError_t launch_f32_to_f16(const float* x, size_t n, __half* y, cudaStream_t s) {
-  f32_to_f16_kernel<<<grid_for(n), 256, 0, s>>>(x, n, y);
-  return cudaGetLastError();
+  return launch_kernel(f32_to_f16_kernel, dim3(grid_for(n)), dim3(256), 0, s, 0, x, n, y);
 }
 
 cudaError_t launch_cfg_lcm(const float* eps2, float* latents, const float* noise, int n_img, int L, float cfg,
                            double c_skip, double c_out, double sa, double sb, double sap, double sbp, int last,
                            float* lat_pair, cudaStream_t s) {
   const size_t total = (size_t)n_img * L;
-  cfg_lcm_kernel<<<grid_for(total), 256, 0, s>>>(eps2, latents, noise, n_img, L, cfg, c_skip, c_out, sa, sb, sap, sbp,
-                                                 last, lat_pair);
-  return cudaGetLastError();
+  return launch_kernel(cfg_lcm_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, eps2, latents, noise, n_img, L, cfg,
+                       c_skip, c_out, sa, sb, sap, sbp, last, lat_pair);
 }
 
 }  // namespace sdg

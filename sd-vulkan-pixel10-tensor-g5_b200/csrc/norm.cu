@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "sdg_kernels.h"
+#include "sdg_launch.h"
 #include "sdg_ptx.cuh"
 
 namespace sdg {
@@ -66,6 +67,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // one block per (group, image): exact mean / centred variance -> (mu, rstd)
 __global__ void __launch_bounds__(kGnStatThreads) gn_stats_kernel(GroupNormArgs a, float2* __restrict__ gstat) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[40];
   const int C = a.C0 + a.C1;
   const int g = blockIdx.x, img = blockIdx.y;
@@ -97,6 +100,8 @@ __global__ void __launch_bounds__(kGnStatThreads) gn_stats_kernel(GroupNormArgs 
 }
 
 __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, int ppb, const float2* __restrict__ gstat) {
+  pdl_wait();
+  pdl_trigger();
   const int C = a.C0 + a.C1;
   const int cpg = C / a.groups;
   const int img = blockIdx.y;
@@ -139,16 +144,28 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
 // Each CTA owns 1/K of the image's pixels for a slice of whole groups. Every
 // thread issues all loads of its share of the chunk up front (at most kGnMaxV
 // 16-byte vectors, kept in registers: high memory-level parallelism, one
-// global read per element). Group sums (pass 1, mean) and centred sums of
-// squares (pass 2, variance) are exchanged through distributed shared memory
-// and summed in rank order (deterministic, exact two-pass); pass 3 normalises
-// from registers. Rank 0 also records (mean, rstd) per group.
-constexpr int kGnMaxCluster = 16;  // non-portable size, opted in at launch
-constexpr int kGnFusedThreads = 512;
-constexpr int kGnMaxV = 8;
+// global read per element). Each CTA reduces its own chunk exactly (two
+// passes: mean, then centred sum of squares, both over registers); the K
+// per-CTA (mean, M2) pairs are exchanged once through distributed shared
+// memory and merged in rank order with the pairwise update of Chan, Golub and
+// LeVeque (deterministic). A third pass normalises from registers. Rank 0
+// also records (mean, rstd) per group.
+// Clusters of up to 8 CTAs (the portable size) where the shape allows: a
+// 16-CTA cluster needs 16 free SMs inside one GPC, and at one 512-thread CTA
+// per SM only 7 such clusters fit on a B200 at once. 16 (non-portable, opted
+// in at launch) only for shapes no smaller cluster can hold.
+constexpr int kGnMaxCluster = 16;
+constexpr int kGnPreferredCluster = 8;
+constexpr int kGnFusedThreads = 256;  // two CTAs per SM
+constexpr int kGnMaxV = 16;
 
-__global__ void __launch_bounds__(kGnFusedThreads)
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kGnFusedThreads, 2)
     gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
+  pdl_wait();
+  pdl_trigger();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -165,10 +182,12 @@ __global__ void __launch_bounds__(kGnFusedThreads)
   const int chunk = (a.HW + kc - 1) / kc;
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
-  __shared__ float red[4096];        // [rows][Ws] per-channel partials (rows * Ws <= 4096)
+  __shared__ float red[kGnFusedThreads * 8];  // [rows][Ws] per-channel partials (rows * Ws <= threads * 8)
   __shared__ float red2[kGnFusedThreads];  // [row slice][Ws] (slices * Ws <= threads)
   __shared__ float chan[320];        // per-channel CTA sums
-  __shared__ float part[2][32];      // per-group partials of this CTA, read by the whole cluster
+  __shared__ float gsum[32];         // per-group CTA sums
+  __shared__ float2 part[32];        // this CTA's (mean, M2) per group, read by the whole cluster
+  __shared__ float2 allp[kGnMaxCluster][32];
   __shared__ float gmu[32], grs[32];
   __shared__ float sc[320], sh[320];
   const int t = threadIdx.x;
@@ -176,7 +195,7 @@ __global__ void __launch_bounds__(kGnFusedThreads)
   const bool active = r < rows;
   const int c0 = cbeg + v * 8;       // first channel of this thread's vector
   const int cnt = (active && p0 + r < p1) ? (p1 - p0 - r + rows - 1) / rows : 0;
-  const float N = (float)a.HW * cpg;
+  const float n_loc = (float)max(0, p1 - p0) * cpg;
 
   uint4 xs[kGnMaxV];
   int cl;
@@ -195,14 +214,13 @@ __global__ void __launch_bounds__(kGnFusedThreads)
       x[2 * e + 1] = f.y;
     }
   };
-  auto reduce_to_groups = [&](const float (&acc)[8], int which) {
+  // per-thread channel partials -> per-group CTA sums in gsum (fixed order)
+  auto cta_group_sums = [&](const float (&acc)[8]) {
     if (active) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) red[r * Ws + v * 8 + e] = acc[e];
     }
     __syncthreads();
-    // rows -> row slices (all threads), slices -> channels, channels -> groups (a warp per group);
-    // every sum in a fixed order (deterministic)
     const int nslc = kGnFusedThreads / Ws;
     if (t < nslc * Ws) {
       const int c = t % Ws, rs = t / Ws;
@@ -221,18 +239,12 @@ __global__ void __launch_bounds__(kGnFusedThreads)
       float s = 0.f;
       for (int j = (t & 31); j < cpg; j += 32) s += chan[g * cpg + j];
       for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if ((t & 31) == 0) part[which][g] = s;
-    }
-    cluster.sync();
-    if (t < gps) {
-      float s = 0.f;
-      for (int q = 0; q < kc; ++q) s += cluster.map_shared_rank(&part[which][0], q)[t];
-      if (which == 0) gmu[t] = s / N;
-      else grs[t] = rsqrtf(s / N + a.eps);
+      if ((t & 31) == 0) gsum[g] = s;
     }
     __syncthreads();
   };
 
+  // pass 1: this CTA's group means
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -245,10 +257,15 @@ __global__ void __launch_bounds__(kGnFusedThreads)
       for (int e = 0; e < 8; ++e) acc[e] += x[e];
     }
   }
-  reduce_to_groups(acc, 0);
+  cta_group_sums(acc);
   float mu[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) { acc[e] = 0.f; mu[e] = active ? gmu[(v * 8 + e) / cpg] : 0.f; }
+  for (int e = 0; e < 8; ++e) {
+    acc[e] = 0.f;
+    mu[e] = (active && n_loc > 0.f) ? gsum[(v * 8 + e) / cpg] / n_loc : 0.f;
+  }
+  if (t < gps) part[t].x = n_loc > 0.f ? gsum[t] / n_loc : 0.f;
+  // pass 2: centred sums of squares about this CTA's means
 #pragma unroll
   for (int i = 0; i < kGnMaxV; ++i) {
     if (i < cnt) {
@@ -261,7 +278,34 @@ __global__ void __launch_bounds__(kGnFusedThreads)
       }
     }
   }
-  reduce_to_groups(acc, 1);
+  cta_group_sums(acc);
+  if (t < gps) part[t].y = gsum[t];
+  // one exchange: every CTA gathers all K (mean, M2) pairs, then merges them in rank order
+  cluster_arrive();
+  cluster_wait();
+  for (int i = t; i < kc * gps; i += kGnFusedThreads) {
+    const int q = i / gps, g = i - q * gps;
+    allp[q][g] = cluster.map_shared_rank(&part[0], q)[g];
+  }
+  cluster_arrive();  // this CTA no longer reads remote memory; the matching wait is at the end
+  __syncthreads();
+  if (t < gps) {
+    float n = 0.f, m = 0.f, m2 = 0.f;
+    for (int q = 0; q < kc; ++q) {
+      const int q0 = q * chunk, q1 = min(a.HW, q0 + chunk);
+      const float nb = (float)max(0, q1 - q0) * cpg;
+      if (nb <= 0.f) continue;
+      const float2 pb = allp[q][t];
+      const float nn = n + nb;
+      const float d = pb.x - m;
+      m += d * (nb / nn);
+      m2 += pb.y + d * d * (n * nb / nn);
+      n = nn;
+    }
+    gmu[t] = m;
+    grs[t] = rsqrtf(m2 / n + a.eps);
+  }
+  __syncthreads();
   if (rank == 0 && t < gps && gstat) gstat[img * a.groups + slice * gps + t] = make_float2(gmu[t], grs[t]);
   for (int c = t; c < Ws; c += blockDim.x) {
     const int g = c / cpg;
@@ -293,35 +337,53 @@ __global__ void __launch_bounds__(kGnFusedThreads)
       }
     }
   }
-  cluster.sync();  // no CTA leaves while another may still read its `part`
+  cluster_wait();  // no CTA leaves while another may still read its `part`
 }
 
-// Cluster size for a (slice, image): ~40 KB of input per CTA, at most 16, and
-// small enough that each thread's share of the chunk fits kGnMaxV vectors.
-int gn_cluster_ctas(int HW, int Ws) {
+// Cluster size for a (slice, image): ~20 KB of input per CTA, at most `maxc`,
+// and large enough that each thread's share of the chunk fits kGnMaxV vectors.
+int gn_cluster_ctas(int HW, int Ws, int maxc = kGnPreferredCluster) {
   const int rows = kGnFusedThreads / (Ws / 8);
   const long bytes = (long)HW * Ws * 2;
-  int k = (int)std::min<long>(kGnMaxCluster, std::max<long>(1, (bytes + 40959) / 40960));
+  int k = (int)std::min<long>(maxc, std::max<long>(1, (bytes + 20479) / 20480));
   int pow2 = 1;
   while (pow2 < k) pow2 *= 2;
   k = pow2;
-  while (k <= kGnMaxCluster && ((HW + k - 1) / k + rows - 1) / rows > kGnMaxV) k *= 2;
-  return k <= kGnMaxCluster ? k : 0;
+  while (k <= maxc && ((HW + k - 1) / k + rows - 1) / rows > kGnMaxV) k *= 2;
+  return k <= maxc ? k : 0;
 }
 
-// Largest slice count (dividing the group count) whose slice keeps whole
-// 8-channel vectors and at least 64 channels per pixel row and fits a cluster;
-// 0 if none fits.
-int gn_fused_slices(int C, int groups, int HW) {
-  int best = 0;
+// Slice count (dividing the group count; whole groups and whole 8-channel
+// vectors per slice) for the fused kernel: the one giving the most CTAs per
+// image up to ~72 (so a batch of 2 stays within one wave of 148 SMs), among
+// slices of at least 40 channels when any fits; 0 if none fits.
+int gn_fused_slices(int C, int groups, int HW, int maxc = kGnPreferredCluster) {
+  int best = 0, best_ctas = 0;
+  bool best_wide = false;
   for (int ns = 1; ns <= groups; ns *= 2) {
     if (groups % ns || C % ns) continue;
     const int Ws = C / ns;
-    if (Ws % 8 || Ws > 320 || (Ws % (C / groups)) || Ws / (C / groups) > 32) continue;
-    if (gn_cluster_ctas(HW, Ws) == 0) continue;
-    if (Ws >= 64 || best == 0) best = ns;
+    if (Ws % 8 || Ws > 256 || (Ws % (C / groups)) || Ws / (C / groups) > 32) continue;
+    const int k = gn_cluster_ctas(HW, Ws, maxc);
+    if (k == 0) continue;
+    const int ctas = ns * k;
+    const bool wide = Ws >= 40;
+    if (best == 0 || (wide && !best_wide) ||
+        (wide == best_wide && ((ctas <= 72 && ctas > best_ctas) || (best_ctas > 72 && ctas < best_ctas)))) {
+      best = ns;
+      best_ctas = ctas;
+      best_wide = wide;
+    }
   }
+  if (best == 0 && maxc < kGnMaxCluster) return gn_fused_slices(C, groups, HW, kGnMaxCluster);
   return best;
+}
+
+// Cluster size used with gn_fused_slices' choice.
+int gn_fused_cluster(int C, int groups, int HW, int ns) {
+  const int k = gn_cluster_ctas(HW, C / ns, kGnPreferredCluster);
+  if (k && gn_fused_slices(C, groups, HW, kGnPreferredCluster) == ns) return k;
+  return gn_cluster_ctas(HW, C / ns, kGnMaxCluster);
 }
 
 // LayerNorm over C per token: one warp per token, values kept in registers,
@@ -329,6 +391,8 @@ int gn_fused_slices(int C, int groups, int HW) {
 template <int VPL>  // 8-channel vectors per lane
 __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, int M, int C, const float* __restrict__ g,
                                                  const float* __restrict__ b, float eps, __half* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= M) return;
@@ -375,13 +439,17 @@ __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, i
   for (int i = 0; i < VPL; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nvec) {
+      const float4* g4 = reinterpret_cast<const float4*>(g + vi * 8);
+      const float4* b4 = reinterpret_cast<const float4*>(b + vi * 8);
+      const float4 ga = __ldg(g4), gb = __ldg(g4 + 1), ba = __ldg(b4), bb = __ldg(b4 + 1);
+      const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
       uint4 o;
       uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c = vi * 8 + 2 * e;
-        ow[e] = pack_half2((v[i * 8 + 2 * e] - mu) * rs * g[c] + b[c], (v[i * 8 + 2 * e + 1] - mu) * rs * g[c + 1] + b[c + 1]);
-      }
+      for (int e = 0; e < 4; ++e)
+        ow[e] = pack_half2((v[i * 8 + 2 * e] - mu) * rs * gg[2 * e] + bt[2 * e],
+                           (v[i * 8 + 2 * e + 1] - mu) * rs * gg[2 * e + 1] + bt[2 * e + 1]);
       *reinterpret_cast<uint4*>(yr + vi * 8) = o;
     }
   }
@@ -418,40 +486,25 @@ cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
     cluster_ok[dev] = true;
   }
   if (ns > 0) {
-    const int kc = gn_cluster_ctas(a.HW, C / ns);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ns * kc, a.B);
-    cfg.blockDim = dim3(kGnFusedThreads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kc;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gn_fused_kernel, a, ns, gstat);
+    const int kc = gn_fused_cluster(C, a.groups, a.HW, ns);
+    return launch_kernel(gn_fused_kernel, dim3(ns * kc, a.B), dim3(kGnFusedThreads), 0, s, kc, a, ns, gstat);
   }
-  gn_stats_kernel<<<dim3(a.groups, a.B), kGnStatThreads, 0, s>>>(a, gstat);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(gn_stats_kernel, dim3(a.groups, a.B), dim3(kGnStatThreads), 0, s, 0, a, gstat);
   if (e != cudaSuccess) return e;
   const int ppb = gn_ppb(a.HW, C);
   const int nblk = (a.HW + ppb - 1) / ppb;
-  gn_apply_kernel<<<dim3(nblk, a.B), kGnThreads, 0, s>>>(a, ppb, gstat);
-  return cudaGetLastError();
+  return launch_kernel(gn_apply_kernel, dim3(nblk, a.B), dim3(kGnThreads), 0, s, 0, a, ppb,
+                       (const float2*)gstat);
 }
 
 cudaError_t launch_layernorm(const __half* x, int M, int C, const float* g, const float* b, float eps, __half* y,
                              cudaStream_t s) {
   if (C % 8 || C > 2048 || M <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b)) & 15) return cudaErrorInvalidValue;
   const int nvec = C / 8;
   const int blocks = (M * 32 + 255) / 256;
-  if (nvec <= 32) ln_kernel<1><<<blocks, 256, 0, s>>>(x, M, C, g, b, eps, y);
-  else if (nvec <= 64) ln_kernel<2><<<blocks, 256, 0, s>>>(x, M, C, g, b, eps, y);
-  else if (nvec <= 128) ln_kernel<4><<<blocks, 256, 0, s>>>(x, M, C, g, b, eps, y);
-  else ln_kernel<8><<<blocks, 256, 0, s>>>(x, M, C, g, b, eps, y);
-  return cudaGetLastError();
+  auto k = nvec <= 32 ? ln_kernel<1> : nvec <= 64 ? ln_kernel<2> : nvec <= 128 ? ln_kernel<4> : ln_kernel<8>;
+  return launch_kernel(k, dim3(blocks), dim3(256), 0, s, 0, x, M, C, g, b, eps, y);
 }
 
 }  // namespace sdg

@@ -39,6 +39,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+// Programmatic dependent launch. Every kernel of this library is launched
+// with programmatic stream serialization (launch_kernel) and calls pdl_wait()
+// before its first global memory access, so its launch and prologue overlap
+// the previous kernel's tail; pdl_trigger() lets the next kernel be scheduled.
+// Every kernel waits on every path, which keeps the ordering transitive.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

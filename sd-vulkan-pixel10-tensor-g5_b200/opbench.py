@@ -46,6 +46,13 @@ def build_ops(sdg, dev):
         y = torch.empty_like(x)
         ops[f"conv3x3_{C}_{H}"] = (lambda x=x, w=w, b=b, y=y, ws=ws, C=C: sdg.conv2d(x, w, b, C, out=y, workspace=ws),
                                     2.0 * B * H * H * C * 9 * C, 0.0)
+    for M, N, K in ((8192, 320, 2880), (8192, 1280, 1280), (8192, 4096, 4096), (1024, 320, 2880), (2048, 320, 2880),
+                    (4096, 320, 2880)):                                     # plain GEMMs vs cuBLAS
+        xa = rn(M, K)
+        wa = rn(N, K, std=0.02)
+        ya = torch.empty((M, N), dtype=torch.float16, device=dev)
+        ops[f"linear_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ya=ya: sdg.linear(xa, wa, out=ya), 2.0 * M * N * K, 0.0)
+        ops[f"cublas_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ya=ya: torch.matmul(xa, wa.t(), out=ya), 2.0 * M * N * K, 0.0)
     x = rn(B, 32, 32, 320)                                                  # config 1 conv1x1 skip
     w = rn(640, 320, std=0.02)
     y = torch.empty((B, 32, 32, 640), dtype=torch.float16, device=dev)
@@ -59,6 +66,16 @@ def build_ops(sdg, dev):
         ops[f"gn_silu_{C}_{H}"] = (lambda xg=xg, gm=gm, bt=bt, yg=yg, st=st: sdg.groupnorm(xg, gm, bt, 1e-5, True, out=yg,
                                                                                         stats=st),
                                    0.0, 2.0 * 2 * B * H * H * C)
+    for M, C in ((8192, 320), (2048, 640), (512, 1280)):                    # transformer LayerNorm
+        xl = rn(M, C)
+        gl = torch.ones(C, device=dev)
+        bl = torch.zeros(C, device=dev)
+        yl = torch.empty_like(xl)
+        ops[f"layernorm_{M}_{C}"] = (lambda xl=xl, gl=gl, bl=bl, yl=yl: sdg.layernorm(xl, gl, bl, out=yl), 0.0,
+                                     2.0 * 2 * M * C)
+    xt = rn(64)
+    yt = torch.empty_like(xt)
+    ops["launch_floor_add64"] = (lambda: sdg.add(xt, xt, out=yt), 0.0, 0.0)   # per-launch floor in a graph
     heads = 8                                                               # config 2 attention
     for name, Sq, Sk, d in (("attn_self_4096_d40", 4096, 4096, 40), ("attn_self_1024_d80", 1024, 1024, 80),
                             ("attn_self_256_d160", 256, 256, 160), ("attn_cross_4096_d40", 4096, 77, 40),
@@ -115,6 +132,9 @@ def main():
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000.0 / a.iters
         rec = {"op": n, "us": round(us, 2)}
+        if not flops and not nbytes:
+            rec["note"] = "per-launch time of a trivial kernel"
+
         if flops:
             rec["tflops"] = round(flops / us / 1e6, 1)
             rec["frac_of_tensor_peak"] = round(flops / us / 1e6 / tc, 3)
