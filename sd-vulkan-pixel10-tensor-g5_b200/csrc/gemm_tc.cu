@@ -61,13 +61,21 @@ struct GemmDev {
   int* err;
 };
 
-template <int BN, bool W8>
+// PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2: each CTA loads its own 128 A rows and half of the
+// BN W rows, the even CTA issues the MMAs, and each CTA's TMEM receives its
+// 128 rows of the accumulator. Per CTA this halves the W bytes moved per MMA.
+template <int BN, bool W8, bool PAIR = false>
 struct Cfg {
+  static_assert(!(W8 && PAIR), "weight-only int8 tiles use single-CTA kernels");
   static constexpr int kThreads = W8 ? 320 : 192;
-  static constexpr uint32_t kBTileBytes = BN * BK * 2;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;  // W rows held by this CTA
+  static constexpr uint32_t kBTileBytes = kBRows * BK * 2;
   static constexpr uint32_t kB8Bytes = W8 ? BN * BK : 0;  // int8 staging tile
   static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes + kB8Bytes;
-  static constexpr uint32_t kTxBytes = kATileBytes + (W8 ? kB8Bytes : kBTileBytes);  // bytes TMA delivers per stage
+  // bytes TMA delivers per stage (PAIR: counted on the even CTA's barrier for both CTAs)
+  static constexpr uint32_t kTxBytes =
+      PAIR ? 2 * (kATileBytes + kBTileBytes) : kATileBytes + (W8 ? kB8Bytes : kBTileBytes);
   // as many stages as shared memory holds: TMA latency from L2 needs deep pipelines
   static constexpr int kStages = (232448 - 1024 - 512) / kStageBytes > 12 ? 12 : (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kAccStride = BN <= 16 ? 16 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
@@ -166,11 +174,15 @@ __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& h
   hi = *reinterpret_cast<uint32_t*>(&hb);
 }
 
-template <int BN, bool W8>
-__global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
+template <int BN, bool W8, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_w, const GemmDev p) {
-  using C = Cfg<BN, W8>;
+  using C = Cfg<BN, W8, PAIR>;
+  constexpr int TM = PAIR ? 2 * BM : BM;  // output rows per unit
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int team = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // pair (or CTA) index
+  const int nteams = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -191,7 +203,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * S + 4);
   auto conv_bar = [&](int s) { return bar0 + 8u * (2 * S + 5 + s); };
 
-  const int num_m = (p.M + BM - 1) / BM;
+  const int num_m = (p.M + TM - 1) / TM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_mn = num_m * num_n;
   const int num_units = num_mn * p.splits;
@@ -214,7 +226,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), PAIR ? 8 : 4);  // epilogue warps of both CTAs arrive on the even CTA's
     }
     mbar_init(drain_bar, 1);
     if constexpr (W8)
@@ -227,11 +239,20 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
     if (p.cin1 > 0) tma_prefetch_desc(&map_a1);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc2(smem_u32(tmem_slot), C::kTmemCols);
+      tmem_relinquish2();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA signal
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // the previous kernel's outputs are visible from here on
@@ -245,10 +266,11 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
       bool issued[S];
       for (int s = 0; s < S; ++s) { issued[s] = false; last_phase[s] = 0; }
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      for (int unit = team; unit < num_units && ok; unit += nteams) {
         int m_blk, n_blk, kb0, kb1;
         decode(unit, m_blk, n_blk, kb0, kb1);
-        const int m0 = m_blk * BM, n0 = n_blk * BN;
+        const int m0 = m_blk * TM + (int)rank * BM;          // this CTA's A rows
+        const int n0 = n_blk * BN + (int)rank * C::kBRows;   // this CTA's W rows
         int img0 = 0, y0 = 0;
         if (p.taps == 9) {
           const int hw = p.H * p.W;
@@ -259,9 +281,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
           issued[s] = true;
           last_phase[s] = ph;
+          const uint32_t fb = PAIR ? mapa_shared(full_bar(s), 0) : full_bar(s);
           const uint32_t dA = smem_u32(sA + s * kATileBytes);
           const uint32_t dB = W8 ? smem_u32(sB8 + s * C::kB8Bytes) : smem_u32(sB + s * C::kBTileBytes);
           const int tap = kb / kb_per_tap;
@@ -269,32 +292,49 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
           const bool second = cc >= p.cin0;
           const CUtensorMap* ma = second ? &map_a1 : &map_a0;
           const int ch = second ? cc - p.cin0 : cc;
-          if (p.taps == 9) {
-            const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-            tma_load_4d(dA, ma, full_bar(s), ch, dx, y0 + dy, img0);
+          if constexpr (PAIR) {
+            if (p.taps == 9) {
+              const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+              tma_load_4d_pair(dA, ma, fb, ch, dx, y0 + dy, img0);
+            } else {
+              tma_load_2d_pair(dA, ma, fb, ch, m0);
+            }
+            tma_load_2d_pair(dB, &map_w, fb, kb * BK, n0);
           } else {
-            tma_load_2d(dA, ma, full_bar(s), ch, m0);
+            if (p.taps == 9) {
+              const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+              tma_load_4d(dA, ma, fb, ch, dx, y0 + dy, img0);
+            } else {
+              tma_load_2d(dA, ma, fb, ch, m0);
+            }
+            tma_load_2d(dB, &map_w, fb, kb * BK, n0);
           }
-          tma_load_2d(dB, &map_w, full_bar(s), kb * BK, n0);
         }
       }
       if (!ok) {
-        // abort path: wait (bounded) for every copy this thread put in flight
-        for (int s = 0; s < S; ++s)
-          if (issued[s]) mbar_wait(full_bar(s), (uint32_t)last_phase[s], p.err, kDevTimeoutDrain);
+        // abort path: wait (bounded) for every copy this thread put in flight; the odd
+        // CTA of a pair cannot observe the even CTA's barrier and waits out a fixed time
+        if (rank == 0) {
+          for (int s = 0; s < S; ++s)
+            if (issued[s]) mbar_wait(full_bar(s), (uint32_t)last_phase[s], p.err, kDevTimeoutDrain);
+        } else {
+          spin_ns(200000);
+        }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(BM, BN, false);
+    // ------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16(TM, BN, false);
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x, ++tl) {
+      for (int unit = team; unit < num_units && ok; unit += nteams, ++tl) {
         int m_blk, n_blk, kb0, kb1;
         decode(unit, m_blk, n_blk, kb0, kb1);
         const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
-        if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc)) { ok = false; break; }
+        const bool got = PAIR ? mbar_wait_cluster(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc)
+                              : mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc);
+        if (!got) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -306,22 +346,35 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
           const uint64_t da = sdesc_sw128(smem_u32(sA + s * kATileBytes), 16, 1024);
           const uint64_t db = sdesc_sw128(smem_u32(sB + s * C::kBTileBytes), 16, 1024);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-          mma_commit(empty_bar(s));
+          for (int k = 0; k < BK / 16; ++k) {
+            if constexpr (PAIR)
+              mma_f16_ss2(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          if constexpr (PAIR)
+            mma_commit2_mc(empty_bar(s), 0x3);  // frees stage s in both CTAs
+          else
+            mma_commit(empty_bar(s));
         }
         if (!ok) break;
-        mma_commit(tfull_bar(acc));
+        if constexpr (PAIR)
+          mma_commit2_mc(tfull_bar(acc), 0x3);
+        else
+          mma_commit(tfull_bar(acc));
       }
       // every issued MMA has retired before TMEM is released
-      mma_commit(drain_bar);
+      if constexpr (PAIR)
+        mma_commit2_mc(drain_bar, 0x1);
+      else
+        mma_commit(drain_bar);
       mbar_wait(drain_bar, 0, p.err, kDevTimeoutDrain);
     }
   } else if (W8 && warp >= 6) {
     // ------------------------------------------------------------ int8 -> fp16 converters (wo8)
     const int ct = threadIdx.x - 192;  // 0..127
     uint32_t it = 0;
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+    for (int unit = team; unit < num_units; unit += nteams) {
       int m_blk, n_blk, kb0, kb1;
       decode(unit, m_blk, n_blk, kb0, kb1);
       bool ok = true;
@@ -355,14 +408,14 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
     const int lg = warp & 3;  // TMEM lane group this warp may access
     const int row = lg * 32 + lane;
     uint32_t tl = 0;
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++tl) {
+    for (int unit = team; unit < num_units; unit += nteams, ++tl) {
       int m_blk, n_blk, kb0, kb1;
       decode(unit, m_blk, n_blk, kb0, kb1);
       const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int m = m_blk * BM + row;
+      const int m = m_blk * TM + (int)rank * BM + row;
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
@@ -442,15 +495,27 @@ __global__ void __launch_bounds__(Cfg<BN, W8>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (lane == 0) {
+        if (PAIR && rank != 0)
+          mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+        else
+          mbar_arrive(tempty_bar(acc));
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR)
+    cluster_sync_all();  // neither CTA frees TMEM or shared memory the pair still uses
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc2(tmem_base, C::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
@@ -481,22 +546,24 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
   }
 }
 
-template <int BN, bool W8>
+template <int BN, bool W8, bool PAIR>
 cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1, const CUtensorMap& mw,
                       cudaStream_t s) {
-  using C = Cfg<BN, W8>;
+  using C = Cfg<BN, W8, PAIR>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_tc_kernel<BN, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::kSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const int units = ((d.M + BM - 1) / BM) * ((d.N + BN - 1) / BN) * d.splits;
-  const int grid = std::max(1, std::min(units, num_sms()));
-  cudaError_t e = launch_kernel(gemm_tc_kernel<BN, W8>, dim3(grid), dim3(C::kThreads), C::kSmem, s, 0, ma0, ma1, mw, d);
+  constexpr int TM = PAIR ? 2 * BM : BM;
+  const int units = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN) * d.splits;
+  const int teams = std::max(1, std::min(units, PAIR ? num_sms() / 2 : num_sms()));
+  cudaError_t e = launch_kernel(gemm_tc_kernel<BN, W8, PAIR>, dim3(PAIR ? 2 * teams : teams), dim3(C::kThreads),
+                                C::kSmem, s, PAIR ? 2 : 0, ma0, ma1, mw, d);
   if (e != cudaSuccess || d.splits == 1) return e;
   const size_t total = (size_t)d.M * ((d.N + 7) / 8);
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
@@ -505,11 +572,14 @@ cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMa
 
 struct TileChoice {
   int bn = 64, splits = 1, kb_per_split = 1;
+  bool pair = false;  // 256-row tiles on a CTA pair (cta_group::2)
 };
 
 // Cost model (cycles of the slowest CTA): per 64-deep k-block a CTA needs
-// max(MMA cycles, operand bytes / ~64 B per cycle of L2 bandwidth); waves of
-// units over the SMs; plus the split-K reduce traffic.
+// max(MMA cycles, operand bytes it loads / ~64 B per cycle of L2 bandwidth);
+// waves of units over the SMs (CTA pairs: 256-row units over half as many
+// teams, each CTA loading 128 A rows and half the W rows); plus the split-K
+// reduce traffic.
 TileChoice choose_tiles(const GemmArgs& a) {
   TileChoice best;
   const int KB = a.K / BK;
@@ -524,30 +594,38 @@ TileChoice choose_tiles(const GemmArgs& a) {
     best.bn = 16;
     return best;
   }
+  const bool pair_ok = a.w8 == nullptr && a.M > BM;
   if (a.epi == kEpiGeglu) {
     best.bn = 256;
+    best.pair = pair_ok;
     return best;
   }
   const int cands[4] = {256, 160, 128, 64};
   double best_t = 1e30;
-  for (int bn : cands) {
-    if (a.N % bn != 0) continue;
-    const int tiles = num_m * (a.N / bn);
-    const double kcost = std::max(2.0 * bn, (kATileBytes + bn * BK * 2.0) / 64.0);
-    const int max_split = (a.epi == kEpiNchwF32) ? 1 : std::max(1, std::min(32, KB / 6));
-    for (int sp = 1; sp <= max_split; ++sp) {
-      const int kbs = (KB + sp - 1) / sp;
-      const int real_sp = (KB + kbs - 1) / kbs;
-      if (real_sp != sp) continue;
-      const int units = tiles * sp;
-      const int waves = (units + sms - 1) / sms;
-      double t = (double)waves * (kbs * kcost + 600.0);  // + per-unit pipeline fill / epilogue
-      if (sp > 1) t += ((double)sp * a.M * a.N * 4.0 + a.M * a.N * 2.0) / 2500.0 + 3000.0;  // reduce pass
-      if (t < best_t * 0.97) {
-        best_t = t;
-        best.bn = bn;
-        best.splits = sp;
-        best.kb_per_split = kbs;
+  for (int pr = 0; pr < 2; ++pr) {
+    if (pr && !pair_ok) continue;
+    for (int bn : cands) {
+      if (a.N % bn != 0 || (pr && bn == 64)) continue;
+      const int tiles = (pr ? (a.M + 2 * BM - 1) / (2 * BM) : num_m) * (a.N / bn);
+      const int teams = pr ? sms / 2 : sms;
+      const double wrows = pr ? bn / 2 : bn;
+      const double kcost = std::max(2.0 * bn, (kATileBytes + wrows * BK * 2.0) / 64.0);
+      const int max_split = (a.epi == kEpiNchwF32) ? 1 : std::max(1, std::min(32, KB / 6));
+      for (int sp = 1; sp <= max_split; ++sp) {
+        const int kbs = (KB + sp - 1) / sp;
+        const int real_sp = (KB + kbs - 1) / kbs;
+        if (real_sp != sp) continue;
+        const int units = tiles * sp;
+        const int waves = (units + teams - 1) / teams;
+        double t = (double)waves * (kbs * kcost + 600.0);  // + per-unit pipeline fill / epilogue
+        if (sp > 1) t += ((double)sp * a.M * a.N * 4.0 + a.M * a.N * 2.0) / 2500.0 + 3000.0;  // reduce pass
+        if (t < best_t * 0.97) {
+          best_t = t;
+          best.bn = bn;
+          best.splits = sp;
+          best.kb_per_split = kbs;
+          best.pair = pr != 0;
+        }
       }
     }
   }
@@ -644,22 +722,30 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
     if (!make_tmap(&mw, a.w8, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_DATA_TYPE_UINT8))
       return cudaErrorInvalidValue;
     switch (bn) {
-      case 16: return launch_bn<16, true>(d, ma0, ma1, mw, s);
-      case 64: return launch_bn<64, true>(d, ma0, ma1, mw, s);
-      case 128: return launch_bn<128, true>(d, ma0, ma1, mw, s);
-      case 160: return launch_bn<160, true>(d, ma0, ma1, mw, s);
-      case 256: return launch_bn<256, true>(d, ma0, ma1, mw, s);
+      case 16: return launch_bn<16, true, false>(d, ma0, ma1, mw, s);
+      case 64: return launch_bn<64, true, false>(d, ma0, ma1, mw, s);
+      case 128: return launch_bn<128, true, false>(d, ma0, ma1, mw, s);
+      case 160: return launch_bn<160, true, false>(d, ma0, ma1, mw, s);
+      case 256: return launch_bn<256, true, false>(d, ma0, ma1, mw, s);
       default: return cudaErrorInvalidValue;
     }
   }
-  if (!make_tmap_2d(&mw, a.w, a.N, a.K, a.K, bn, BK)) return cudaErrorInvalidValue;
-
+  // W box: the rows one CTA loads (half the tile's N on a CTA pair)
+  if (!make_tmap_2d(&mw, a.w, a.N, a.K, a.K, tc.pair ? bn / 2 : bn, BK)) return cudaErrorInvalidValue;
+  if (tc.pair) {
+    switch (bn) {
+      case 128: return launch_bn<128, false, true>(d, ma0, ma1, mw, s);
+      case 160: return launch_bn<160, false, true>(d, ma0, ma1, mw, s);
+      case 256: return launch_bn<256, false, true>(d, ma0, ma1, mw, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (bn) {
-    case 16: return launch_bn<16, false>(d, ma0, ma1, mw, s);
-    case 64: return launch_bn<64, false>(d, ma0, ma1, mw, s);
-    case 128: return launch_bn<128, false>(d, ma0, ma1, mw, s);
-    case 160: return launch_bn<160, false>(d, ma0, ma1, mw, s);
-    case 256: return launch_bn<256, false>(d, ma0, ma1, mw, s);
+    case 16: return launch_bn<16, false, false>(d, ma0, ma1, mw, s);
+    case 64: return launch_bn<64, false, false>(d, ma0, ma1, mw, s);
+    case 128: return launch_bn<128, false, false>(d, ma0, ma1, mw, s);
+    case 160: return launch_bn<160, false, false>(d, ma0, ma1, mw, s);
+    case 256: return launch_bn<256, false, false>(d, ma0, ma1, mw, s);
     default: return cudaErrorInvalidValue;
   }
 }
