@@ -68,7 +68,10 @@ struct GemmDev {
 template <int BN, bool W8, bool PAIR = false>
 struct Cfg {
   static_assert(!(W8 && PAIR), "weight-only int8 tiles use single-CTA kernels");
-  static constexpr int kThreads = W8 ? 320 : 192;
+  // warps: 0 TMA, 1 MMA, then 8 epilogue warps (two per TMEM lane quadrant, alternating
+  // column chunks), or for wo8 4 epilogue warps + 4 int8 converter warps
+  static constexpr int kThreads = 320;
+  static constexpr int kEpiWarps = W8 ? 4 : 8;
   static constexpr int kBRows = PAIR ? BN / 2 : BN;  // W rows held by this CTA
   static constexpr uint32_t kBTileBytes = kBRows * BK * 2;
   static constexpr uint32_t kB8Bytes = W8 ? BN * BK : 0;  // int8 staging tile
@@ -105,10 +108,16 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 
-// Fused epilogue for 8 consecutive output columns [n, n+8) of row m (m < M).
-// Not used for GEGLU (which pairs two column ranges).
-__device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int n, float (&v)[8]) {
-  const int img = m / p.rows_per_image;
+__device__ __forceinline__ void add8_f32(const float* src, float (&v)[8]) {  // src 16-byte aligned
+  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+  v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+  v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+}
+
+// Fused epilogue for 8 consecutive output columns [n, n+8) of row m (m < M) of
+// image img = m / rows_per_image. Not used for GEGLU (which pairs two column ranges).
+__device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int img, int n, float (&v)[8]) {
   if (p.wscale) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + min(n + j, p.N - 1));
@@ -121,15 +130,8 @@ __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int n, float 
         p.out_f32[((size_t)img * p.N + n + j) * p.rows_per_image + pix] = v[j] + (p.bias ? __ldg(p.bias + n + j) : 0.f);
     return;
   }
-  if (p.bias) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] += __ldg(p.bias + n + j);
-  }
-  if (p.rowbias) {
-    const float* rb = p.rowbias + (size_t)img * p.rowbias_ld + n;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] += __ldg(rb + j);
-  }
+  if (p.bias) add8_f32(p.bias + n, v);
+  if (p.rowbias) add8_f32(p.rowbias + (size_t)img * p.rowbias_ld + n, v);
   if (p.residual) {
     float rv[8];
     load8h(p.residual + (size_t)m * p.ld_res + n, rv);
@@ -226,7 +228,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), PAIR ? 8 : 4);  // epilogue warps of both CTAs arrive on the even CTA's
+      mbar_init(tempty_bar(a), C::kEpiWarps * (PAIR ? 2 : 1));  // epilogue warps of both CTAs arrive on the even CTA's
     }
     mbar_init(drain_bar, 1);
     if constexpr (W8)
@@ -407,6 +409,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int lg = warp & 3;  // TMEM lane group this warp may access
     const int row = lg * 32 + lane;
+    constexpr int kSplit = C::kEpiWarps / 4;  // warps sharing a lane quadrant split its column chunks
+    const int eh = (warp - 2) >> 2;
     uint32_t tl = 0;
     for (int unit = team; unit < num_units; unit += nteams, ++tl) {
       int m_blk, n_blk, kb0, kb1;
@@ -416,6 +420,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int m = m_blk * TM + (int)rank * BM + row;
+      const int img = m / p.rows_per_image;
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
@@ -424,7 +429,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         constexpr int HALF = BN / 2;
         const int nout0 = n_blk * HALF;
 #pragma unroll 1
-        for (int c = 0; c < HALF; c += CH) {
+        for (int c = eh * CH; c < HALF; c += kSplit * CH) {
           uint32_t ra[32], rg[32];
           if constexpr (CH == 32) {
             tmem_ld32(t_row + c, ra);
@@ -460,7 +465,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += CH) {
+        for (int c = eh * CH; c < BN; c += kSplit * CH) {
           uint32_t r[32];
           if constexpr (CH == 32) {
             tmem_ld32(t_row + c, r);
@@ -489,7 +494,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
             float v[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-            epilogue8(p, m, n + g * 8, v);
+            epilogue8(p, m, img, n + g * 8, v);
           }
         }
       }
@@ -542,7 +547,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
       const float4 b = *reinterpret_cast<const float4*>(src + s * plane + 4);
       v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
     }
-    epilogue8(p, m, n, v);
+    epilogue8(p, m, m / p.rows_per_image, n, v);
   }
 }
 
@@ -683,6 +688,9 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
   if (a.w8 && !a.wscale) return cudaErrorInvalidValue;
+  // the epilogue reads bias / per-image bias 8 columns at a time as two float4
+  if ((reinterpret_cast<uintptr_t>(a.bias) | reinterpret_cast<uintptr_t>(a.rowbias)) & 15) return cudaErrorInvalidValue;
+  if (a.rowbias && a.rowbias_ld % 4) return cudaErrorInvalidValue;
 
   CUtensorMap ma0{}, ma1{}, mw{};
   if (a.taps == 9) {
