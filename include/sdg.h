@@ -127,6 +127,17 @@ SDG_API int sdg_unet_forward_cfg(sdg_engine* e, const float* latent, float times
 SDG_API int sdg_lcm_denoise(sdg_engine* e, const float* latents, const float* cond, const float* uncond,
                             const float* step_noise, int n_img, int H, int W, int steps, float cfg, float* out);
 
+/* sdg_lcm_denoise with classifier-free guidance on the first cfg_steps steps
+ * only (TpuUnetPipeline.kt:75-112: the reference's default is 2 of 4); the
+ * other steps run one cond-only forward per image (batch n_img) and use its
+ * eps directly. cfg <= 1 means no guidance at all (uncond may then be NULL).
+ * cfg_steps >= steps is sdg_lcm_denoise. Within one call every step after a
+ * forward plan's first run reuses that plan's cross-attention K/V (the
+ * context does not change between steps). */
+SDG_API int sdg_lcm_denoise_ex(sdg_engine* e, const float* latents, const float* cond, const float* uncond,
+                               const float* step_noise, int n_img, int H, int W, int steps, float cfg, int cfg_steps,
+                               float* out);
+
 /* Per-category device times of one eager forward (replaces
  * Java_..._unetProfile, vk_engine.cpp:854-872, which only logs). Returns the
  * number of rows written (<= cap) or a negative status. */

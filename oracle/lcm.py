@@ -61,19 +61,28 @@ class LcmScheduler:
 
 
 def cfg_denoise(unet: Callable[[np.ndarray, float, np.ndarray], np.ndarray], latents: np.ndarray, cond: np.ndarray,
-                uncond: np.ndarray, step_noise: Optional[np.ndarray], steps: int = 4, cfg: float = 1.5) -> np.ndarray:
+                uncond: Optional[np.ndarray], step_noise: Optional[np.ndarray], steps: int = 4, cfg: float = 1.5,
+                cfg_steps: Optional[int] = None) -> np.ndarray:
     """Batch-CFG LCM loop over n images (VulkanUnetPipeline.kt:76-90).
 
     unet(lat [B,4,H,W], t, ctx [B,77,768]) -> eps [B,4,H,W]; per image the
-    forward batch is [cond, uncond]. step_noise: [steps-1, n, 4, H, W]."""
+    forward batch is [cond, uncond]. step_noise: [steps-1, n, 4, H, W].
+    cfg_steps: guidance only on the first cfg_steps steps, cond-only eps after
+    them, none at cfg <= 1 (TpuUnetPipeline.kt:97-104); None = every step."""
     n = latents.shape[0]
     sched = LcmScheduler(steps)
     lat = latents.astype(np.float32).copy()
+    guided_steps = steps if cfg_steps is None else cfg_steps
+    if cfg <= 1.0:
+        guided_steps = 0
     for i, t in enumerate(sched.timesteps):
-        lat2 = np.repeat(lat, 2, axis=0)                                   # [cond, uncond] per image
-        ctx2 = np.stack([cond, uncond], axis=1).reshape((2 * n,) + cond.shape[1:])
-        eps2 = unet(lat2, float(t), ctx2).reshape((n, 2) + lat.shape[1:])
-        eps = eps2[:, 1] + np.float32(cfg) * (eps2[:, 0] - eps2[:, 1])
+        if i >= guided_steps:
+            eps = unet(lat, float(t), cond)
+        else:
+            lat2 = np.repeat(lat, 2, axis=0)                               # [cond, uncond] per image
+            ctx2 = np.stack([cond, uncond], axis=1).reshape((2 * n,) + cond.shape[1:])
+            eps2 = unet(lat2, float(t), ctx2).reshape((n, 2) + lat.shape[1:])
+            eps = eps2[:, 1] + np.float32(cfg) * (eps2[:, 0] - eps2[:, 1])
         noise = None if i == steps - 1 else step_noise[i]
         lat = sched.step(lat, eps, noise)
     return lat

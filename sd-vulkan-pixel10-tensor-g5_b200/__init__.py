@@ -70,6 +70,7 @@ _SIGS = {
     "sdg_unet_forward_device": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
     "sdg_unet_forward_cfg": (_I, [_P, _P, _F, _P, _P, _I, _I, _P]),
     "sdg_lcm_denoise": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P]),
+    "sdg_lcm_denoise_ex": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "sdg_profile": (_I, [_P, _I, _I, _I, ctypes.POINTER(ProfileRow), _I]),
     "sdg_forward_launches": (_I, [_P, _I, _I, _I]),
     "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, ctypes.c_size_t, _P,
@@ -213,16 +214,19 @@ class Engine:
                                          out.ctypes.data))
         return out
 
-    def lcm_denoise(self, latents: np.ndarray, cond: np.ndarray, uncond: np.ndarray, step_noise: Optional[np.ndarray],
-                    steps: int = 4, cfg: float = 1.5) -> np.ndarray:
+    def lcm_denoise(self, latents: np.ndarray, cond: np.ndarray, uncond: Optional[np.ndarray],
+                    step_noise: Optional[np.ndarray], steps: int = 4, cfg: float = 1.5,
+                    cfg_steps: Optional[int] = None) -> np.ndarray:
+        """LCM loop on the device; guidance on the first ``cfg_steps`` steps (all when None)."""
         lat = np.ascontiguousarray(latents, dtype=np.float32)
         n, _, H, W = lat.shape
         out = np.empty_like(lat)
         noise = None if step_noise is None else np.ascontiguousarray(step_noise, dtype=np.float32)
-        check(lib().sdg_lcm_denoise(self._h, lat.ctypes.data, np.ascontiguousarray(cond, np.float32).ctypes.data,
-                                    np.ascontiguousarray(uncond, np.float32).ctypes.data,
-                                    None if noise is None else noise.ctypes.data, n, H, W, steps, float(cfg),
-                                    out.ctypes.data))
+        unc = None if uncond is None else np.ascontiguousarray(uncond, np.float32)
+        check(lib().sdg_lcm_denoise_ex(self._h, lat.ctypes.data, np.ascontiguousarray(cond, np.float32).ctypes.data,
+                                       None if unc is None else unc.ctypes.data,
+                                       None if noise is None else noise.ctypes.data, n, H, W, steps, float(cfg),
+                                       steps if cfg_steps is None else int(cfg_steps), out.ctypes.data))
         return out
 
     def profile(self, B: int = 2, H: int = 64, W: int = 64) -> Dict[str, Tuple[float, int, float, float]]:

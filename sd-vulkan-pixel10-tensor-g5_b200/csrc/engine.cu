@@ -99,6 +99,9 @@ struct Plan {
   size_t arena_bytes = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // the same forward reusing the cross-attention K/V of the previous run (context unchanged)
+  cudaGraph_t graph_cached = nullptr;
+  cudaGraphExec_t exec_cached = nullptr;
   // io
   float* lat_in = nullptr; float* t_in = nullptr; float* tproj_in = nullptr; float* ctx_in = nullptr;
   float* out = nullptr;
@@ -116,6 +119,9 @@ class Builder {
   int launches() const { return launches_; }
   // profiling: per-launch category events
   bool profile = false;
+  // context K/V already in the plan's cross-attention buffers: skip the context conversion and the
+  // K/V projections (their outputs persist in the arena between runs of the same plan)
+  bool ctx_cached = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof;
   double cat_flops[8] = {0}, cat_bytes[8] = {0};  // algorithmic work per category (counted in every mode)
 
@@ -172,7 +178,8 @@ struct Engine {
   ~Engine();
   int prepare();
   int get_plan(int B, int H, int W, int mode, Plan** out);
-  int run_plan(Plan* p, cudaStream_t s);
+  // ctx_cached: reuse the cross-attention K/V left in the plan by its previous run (same context)
+  int run_plan(Plan* p, cudaStream_t s, bool ctx_cached = false);
   int check_dev_err(Plan* p, cudaStream_t s);
 };
 
@@ -641,7 +648,8 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
   ln(tt, t.ln2);
   heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
-  heads(ctx16_, B * kCtxLen, kCtxDim, t.kv2, kCtxLen, cb.k, cb.vt, nullptr, 1, kCtxPad);  // K, V^T from context
+  if (!ctx_cached)
+    heads(ctx16_, B * kCtxLen, kCtxDim, t.kv2, kCtxLen, cb.k, cb.vt, nullptr, 1, kCtxPad);  // K, V^T from context
   attn(ab.q, cb.k, cb.vt, kCtxLen, kCtxPad);                       // cross-attention
   lin(o, C, t.out2, tt, tt);
   ln(tt, t.ln3);
@@ -731,13 +739,16 @@ int Builder::run() {
     check(launch_gemv(te, B, 320, w.t1.w, w.t1.w8, w.t1.ws, w.t1.b, kTemb, 0, 1, t1, kTemb, s_), "time mlp 1",
           kCatGemv, (B + 7) / 8);
     begin_op(kCatGemv);
-    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.w8, w.t2.ws, w.t2.b, kTemb, 0, 0, temb, kTemb, s_), "time mlp 2",
+    // temb's only consumers are the time_emb_proj of every ResNet, each after SiLU: apply it once here
+    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.w8, w.t2.ws, w.t2.b, kTemb, 0, 1, temb, kTemb, s_), "time mlp 2",
           kCatGemv, (B + 7) / 8);
     begin_op(kCatGemv);
-    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_w8, w.tp_ws, w.tp_b, w.tp_N, 1, 0, tp_all_, w.tp_N, s_),
+    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_w8, w.tp_ws, w.tp_b, w.tp_N, 0, 0, tp_all_, w.tp_N, s_),
           "time_emb_proj", kCatGemv, (B + 7) / 8);
-    begin_op(kCatMisc);
-    check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
+    if (!ctx_cached) {
+      begin_op(kCatMisc);
+      check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
+    }
   } else {
     launches_ += 3 + 3 * ((B + 7) / 8);
   }
@@ -806,6 +817,8 @@ Engine::~Engine() {
   for (auto& kv : plans) {
     if (kv.second->exec) cudaGraphExecDestroy(kv.second->exec);
     if (kv.second->graph) cudaGraphDestroy(kv.second->graph);
+    if (kv.second->exec_cached) cudaGraphExecDestroy(kv.second->exec_cached);
+    if (kv.second->graph_cached) cudaGraphDestroy(kv.second->graph_cached);
     if (kv.second->arena) cudaFree(kv.second->arena);
   }
   if (warena) cudaFree(warena);
@@ -850,13 +863,30 @@ int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
     pl->graph = g;
   }
   SDG_CUDA_TRY(cudaGraphInstantiate(&pl->exec, pl->graph, 0));
+  SDG_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+  {
+    Builder b(*this, *pl, false, stream);
+    b.ctx_cached = true;
+    st = b.run();
+    cudaGraph_t g = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(stream, &g);
+    if (st || ce != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGraphExecDestroy(pl->exec);
+      cudaGraphDestroy(pl->graph);
+      cudaFree(pl->arena);
+      return st ? st : fail(SDG_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    }
+    pl->graph_cached = g;
+  }
+  SDG_CUDA_TRY(cudaGraphInstantiate(&pl->exec_cached, pl->graph_cached, 0));
   *out = pl.get();
   plans[key] = std::move(pl);
   return SDG_OK;
 }
 
-int Engine::run_plan(Plan* p, cudaStream_t s) {
-  SDG_CUDA_TRY(cudaGraphLaunch(p->exec, s));
+int Engine::run_plan(Plan* p, cudaStream_t s, bool ctx_cached) {
+  SDG_CUDA_TRY(cudaGraphLaunch(ctx_cached ? p->exec_cached : p->exec, s));
   return SDG_OK;
 }
 
@@ -1073,18 +1103,24 @@ static void lcm_schedule(int steps, std::vector<int>& ts, std::vector<double>& a
   }
 }
 
-SDG_API int sdg_lcm_denoise(sdg_engine* h, const float* latents, const float* cond, const float* uncond,
-                            const float* step_noise, int n_img, int H, int W, int steps, float cfg, float* out) {
+SDG_API int sdg_lcm_denoise_ex(sdg_engine* h, const float* latents, const float* cond, const float* uncond,
+                               const float* step_noise, int n_img, int H, int W, int steps, float cfg, int cfg_steps,
+                               float* out) {
   if (!h) return fail(SDG_ERR_NOT_INIT, "null engine");
-  if (!latents || !cond || !uncond || !out || n_img <= 0 || n_img > 32 || steps <= 0 || steps > 50 ||
-      (steps > 1 && !step_noise))
-    return fail(SDG_ERR_ARG, "lcm: bad arguments (n_img 1..32, steps 1..50)");
+  if (!latents || !cond || !out || n_img <= 0 || n_img > 32 || steps <= 0 || steps > 50 || (steps > 1 && !step_noise) ||
+      cfg_steps < 0)
+    return fail(SDG_ERR_ARG, "lcm: bad arguments (n_img 1..32, steps 1..50, cfg_steps >= 0)");
+  // TpuUnetPipeline.kt:97-104: guidance only on the first cfg_steps steps, none at cfg <= 1
+  if (cfg <= 1.0f) cfg_steps = 0;
+  cfg_steps = std::min(cfg_steps, steps);
+  if (cfg_steps > 0 && !uncond) return fail(SDG_ERR_ARG, "lcm: uncond is required for guided steps");
   Engine& e = h->e;
   cudaSetDevice(e.device);
-  const int B = 2 * n_img;
-  sdg::Plan* p = nullptr;
-  int st = e.get_plan(B, H, W, 0, &p);
-  if (st) return st;
+  sdg::Plan* pp = nullptr;  // [cond ; uncond] pairs, batch 2 n_img
+  sdg::Plan* pc = nullptr;  // cond only, batch n_img
+  int st = SDG_OK;
+  if (cfg_steps > 0 && (st = e.get_plan(2 * n_img, H, W, 0, &pp))) return st;
+  if (cfg_steps < steps && (st = e.get_plan(n_img, H, W, 0, &pc))) return st;
   cudaStream_t s = e.stream;
   const size_t L = (size_t)4 * H * W, CT = (size_t)77 * 768;
   // device state: latents [n_img, L] and the step noise [steps-1, n_img, L]
@@ -1093,50 +1129,73 @@ SDG_API int sdg_lcm_denoise(sdg_engine* h, const float* latents, const float* co
   const size_t nn = steps > 1 ? (size_t)(steps - 1) * n_img * L : 1;
   SDG_CUDA_TRY(cudaMallocAsync(&dlat, (size_t)n_img * L * 4, s));
   SDG_CUDA_TRY(cudaMallocAsync(&dnoise, nn * 4, s));
-  std::vector<float> pair((size_t)B * L), ctx((size_t)B * CT);
-  for (int i = 0; i < n_img; ++i) {
-    memcpy(&pair[(size_t)(2 * i) * L], latents + (size_t)i * L, L * 4);
-    memcpy(&pair[(size_t)(2 * i + 1) * L], latents + (size_t)i * L, L * 4);
-    memcpy(&ctx[(size_t)(2 * i) * CT], cond + (size_t)i * CT, CT * 4);
-    memcpy(&ctx[(size_t)(2 * i + 1) * CT], uncond + (size_t)i * CT, CT * 4);
+  std::vector<float> pair, ctx;
+  if (pp) {
+    pair.resize((size_t)2 * n_img * L);
+    ctx.resize((size_t)2 * n_img * CT);
+    for (int i = 0; i < n_img; ++i) {
+      memcpy(&pair[(size_t)(2 * i) * L], latents + (size_t)i * L, L * 4);
+      memcpy(&pair[(size_t)(2 * i + 1) * L], latents + (size_t)i * L, L * 4);
+      memcpy(&ctx[(size_t)(2 * i) * CT], cond + (size_t)i * CT, CT * 4);
+      memcpy(&ctx[(size_t)(2 * i + 1) * CT], uncond + (size_t)i * CT, CT * 4);
+    }
   }
-  int rc = SDG_OK;
+  std::vector<int> ts;
+  std::vector<double> ac;
+  lcm_schedule(steps, ts, ac);
+  // every step's timesteps up front (pinned-free: the host vectors outlive the synchronisation below)
+  std::vector<float> tv((size_t)steps * 2 * n_img);
+  for (int i = 0; i < steps; ++i)
+    for (int b = 0; b < 2 * n_img; ++b) tv[(size_t)i * 2 * n_img + b] = (float)ts[i];
   auto run = [&]() -> int {
     SDG_CUDA_TRY(cudaMemcpyAsync(dlat, latents, (size_t)n_img * L * 4, cudaMemcpyHostToDevice, s));
     if (steps > 1) SDG_CUDA_TRY(cudaMemcpyAsync(dnoise, step_noise, nn * 4, cudaMemcpyHostToDevice, s));
-    SDG_CUDA_TRY(cudaMemcpyAsync(p->lat_in, pair.data(), pair.size() * 4, cudaMemcpyHostToDevice, s));
-    SDG_CUDA_TRY(cudaMemcpyAsync(p->ctx_in, ctx.data(), ctx.size() * 4, cudaMemcpyHostToDevice, s));
-    std::vector<int> ts;
-    std::vector<double> ac;
-    lcm_schedule(steps, ts, ac);
-    std::vector<float> tv(B);
+    if (pp) SDG_CUDA_TRY(cudaMemcpyAsync(pp->ctx_in, ctx.data(), ctx.size() * 4, cudaMemcpyHostToDevice, s));
+    if (pc) SDG_CUDA_TRY(cudaMemcpyAsync(pc->ctx_in, cond, (size_t)n_img * CT * 4, cudaMemcpyHostToDevice, s));
+    if (cfg_steps > 0)
+      SDG_CUDA_TRY(cudaMemcpyAsync(pp->lat_in, pair.data(), pair.size() * 4, cudaMemcpyHostToDevice, s));
+    else
+      SDG_CUDA_TRY(cudaMemcpyAsync(pc->lat_in, latents, (size_t)n_img * L * 4, cudaMemcpyHostToDevice, s));
+    bool used_pp = false, used_pc = false;
     for (int i = 0; i < steps; ++i) {
+      const bool guided = i < cfg_steps;
+      sdg::Plan* p = guided ? pp : pc;
       const int t = ts[i];
-      for (int b = 0; b < B; ++b) tv[b] = (float)t;
-      SDG_CUDA_TRY(cudaMemcpyAsync(p->t_in, tv.data(), B * 4, cudaMemcpyHostToDevice, s));
-      int r = e.run_plan(p, s);
+      SDG_CUDA_TRY(cudaMemcpyAsync(p->t_in, &tv[(size_t)i * 2 * n_img], (size_t)p->B * 4, cudaMemcpyHostToDevice, s));
+      // the context is the same for every step of this call: after a plan's first run its
+      // cross-attention K/V are reused
+      bool& used = guided ? used_pp : used_pc;
+      int r = e.run_plan(p, s, used);
       if (r) return r;
+      used = true;
       const double aT = ac[t], bT = 1.0 - aT, stt = t * 10.0, sd2 = 0.25;
       const double c_skip = sd2 / (stt * stt + sd2), c_out = stt / sqrt(stt * stt + sd2);
       const bool last = i == steps - 1;
       const double aP = last ? 1.0 : ac[ts[i + 1]];
-      SDG_CUDA_TRY(sdg::launch_cfg_lcm(p->out, dlat, last ? nullptr : dnoise + (size_t)i * n_img * L, n_img, (int)L, cfg,
-                                       c_skip, c_out, sqrt(aT), sqrt(bT), sqrt(aP), sqrt(1.0 - aP), last ? 1 : 0,
-                                       last ? nullptr : p->lat_in, s));
-      // the copy of pair/ctx/timesteps above came from pageable host memory;
-      // tv is reused, so make the copy of this step complete before rewriting it
-      SDG_CUDA_TRY(cudaStreamSynchronize(s));
+      const bool next_guided = !last && i + 1 < cfg_steps;
+      float* lat_next = last ? nullptr : (next_guided ? pp->lat_in : pc->lat_in);
+      SDG_CUDA_TRY(sdg::launch_cfg_lcm(p->out, guided ? 1 : 0, dlat, last ? nullptr : dnoise + (size_t)i * n_img * L,
+                                       n_img, (int)L, cfg, c_skip, c_out, sqrt(aT), sqrt(bT), sqrt(aP),
+                                       sqrt(1.0 - aP), last ? 1 : 0, lat_next, next_guided ? 1 : 0, s));
     }
     SDG_CUDA_TRY(cudaMemcpyAsync(out, dlat, (size_t)n_img * L * 4, cudaMemcpyDeviceToHost, s));
     int r = sdg::sync_with_deadline(s, kHostDeadlineS * steps);
     if (r) return r;
-    return e.check_dev_err(p, s);
+    if (pp && (r = e.check_dev_err(pp, s))) return r;
+    if (pc && (r = e.check_dev_err(pc, s))) return r;
+    return SDG_OK;
   };
-  rc = run();
+  const int rc = run();
   cudaFreeAsync(dlat, s);
   cudaFreeAsync(dnoise, s);
   cudaStreamSynchronize(s);
   return rc;
+}
+
+SDG_API int sdg_lcm_denoise(sdg_engine* h, const float* latents, const float* cond, const float* uncond,
+                            const float* step_noise, int n_img, int H, int W, int steps, float cfg, float* out) {
+  if (!uncond) return fail(SDG_ERR_ARG, "lcm: bad arguments (uncond is required)");
+  return sdg_lcm_denoise_ex(h, latents, cond, uncond, step_noise, n_img, H, W, steps, cfg, steps, out);
 }
 
 SDG_API int sdg_forward_launches(sdg_engine* h, int B, int H, int W) {

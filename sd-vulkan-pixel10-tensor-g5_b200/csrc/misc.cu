@@ -37,7 +37,11 @@ __global__ void time_embedding_kernel(const float* t, int n_t, int B, const floa
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvMaxK = 1280;
 
-// One warp per output n; W8 = weight-only int8 rows [N, K] with per-row scale ws[n].
+// Each warp computes kGemvRows outputs n; W8 = weight-only int8 rows [N, K] with
+// per-row scale ws[n]. All of a warp's weight loads are issued before any use
+// (K <= kGemvMaxK: at most kGemvVecs 8-element vectors per lane and row).
+constexpr int kGemvRows = 2;
+constexpr int kGemvVecs = kGemvMaxK / 256;
 template <bool W8>
 __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, int M, int K, const __half* __restrict__ w,
                                                    const int8_t* __restrict__ w8, const float* __restrict__ ws,
@@ -52,46 +56,73 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (n >= N) return;
-  float acc[kGemvMaxM];
+  const int n_first = (blockIdx.x * (blockDim.x >> 5) + warp) * kGemvRows;
+  if (n_first >= N) return;
+  uint4 wv[kGemvRows][kGemvVecs];
 #pragma unroll
-  for (int m = 0; m < kGemvMaxM; ++m) acc[m] = 0.f;
-  for (int k0 = lane * 8; k0 < K; k0 += 256) {
-    float wf[8];
-    if constexpr (W8) {
-      const uint2 u = __ldg(reinterpret_cast<const uint2*>(w8 + (size_t)n * K + k0));
-      const uint32_t b4[2] = {u.x, u.y};
+  for (int r = 0; r < kGemvRows; ++r) {
+    const int n = min(n_first + r, N - 1);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) wf[e] = (float)(int8_t)((b4[e >> 2] >> (8 * (e & 3))) & 0xff);
-    } else {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(w + (size_t)n * K + k0));
-      const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __half22float2(h[e]);
-        wf[2 * e] = f.x;
-        wf[2 * e + 1] = f.y;
+    for (int i = 0; i < kGemvVecs; ++i) {
+      const int k0 = lane * 8 + i * 256;
+      if (k0 < K) {
+        if constexpr (W8) {
+          const uint2 u = __ldg(reinterpret_cast<const uint2*>(w8 + (size_t)n * K + k0));
+          wv[r][i] = make_uint4(u.x, u.y, 0u, 0u);
+        } else {
+          wv[r][i] = __ldg(reinterpret_cast<const uint4*>(w + (size_t)n * K + k0));
+        }
       }
     }
+  }
+  float acc[kGemvRows][kGemvMaxM];
 #pragma unroll
-    for (int m = 0; m < kGemvMaxM; ++m) {
-      if (m < M) {
-        const float* xr = xs + m * K + k0;
+  for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[m] += wf[e] * xr[e];
+    for (int m = 0; m < kGemvMaxM; ++m) acc[r][m] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kGemvVecs; ++i) {
+    const int k0 = lane * 8 + i * 256;
+    if (k0 >= K) break;
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r) {
+      float wf[8];
+      if constexpr (W8) {
+        const uint32_t b4[2] = {wv[r][i].x, wv[r][i].y};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wf[e] = (float)(int8_t)((b4[e >> 2] >> (8 * (e & 3))) & 0xff);
+      } else {
+        const __half2* h = reinterpret_cast<const __half2*>(&wv[r][i]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __half22float2(h[e]);
+          wf[2 * e] = f.x;
+          wf[2 * e + 1] = f.y;
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kGemvMaxM; ++m) {
+        if (m < M) {
+          const float* xr = xs + m * K + k0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r][m] += wf[e] * xr[e];
+        }
       }
     }
   }
 #pragma unroll
-  for (int m = 0; m < kGemvMaxM; ++m) {
-    float v = acc[m];
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0 && m < M) {
-      if constexpr (W8) v *= ws[n];
-      v += bias ? bias[n] : 0.f;
-      if (act_out) v = silu_f(v);
-      y[(size_t)m * ldy + n] = v;
+  for (int r = 0; r < kGemvRows; ++r) {
+    const int n = n_first + r;
+#pragma unroll
+    for (int m = 0; m < kGemvMaxM; ++m) {
+      float v = acc[r][m];
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && m < M && n < N) {
+        if constexpr (W8) v *= ws[n];
+        v += bias ? bias[n] : 0.f;
+        if (act_out) v = silu_f(v);
+        y[(size_t)m * ldy + n] = v;
+      }
     }
   }
 }
@@ -187,25 +218,35 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ x, size_t n, __half*
 // eps = uncond + cfg*(cond-uncond); LCM step (LcmScheduler.kt:68-80, fp64 math
 // like the Kotlin reference); lat_pair[img, 0|1, :] = new latents (input of
 // the next batch-CFG forward).
-__global__ void cfg_lcm_kernel(const float* __restrict__ eps2, float* __restrict__ lat, const float* __restrict__ noise,
-                               int n_img, int L, float cfg, double c_skip, double c_out, double sa, double sb,
-                               double sap, double sbp, int last, float* __restrict__ lat_pair) {
+__global__ void cfg_lcm_kernel(const float* __restrict__ eps, int eps_pairs, float* __restrict__ lat,
+                               const float* __restrict__ noise, int n_img, int L, float cfg, double c_skip,
+                               double c_out, double sa, double sb, double sap, double sbp, int last,
+                               float* __restrict__ lat_next, int next_pairs) {
   pdl_wait();
   pdl_trigger();
   const size_t total = (size_t)n_img * L;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t img = i / L, j = i % L;
-    const float ec = eps2[(img * 2 + 0) * L + j];
-    const float eu = eps2[(img * 2 + 1) * L + j];
-    const float e = eu + cfg * (ec - eu);
+    float e;
+    if (eps_pairs) {
+      const float ec = eps[(img * 2 + 0) * L + j];
+      const float eu = eps[(img * 2 + 1) * L + j];
+      e = eu + cfg * (ec - eu);
+    } else {
+      e = eps[i];
+    }
     const double x = (double)lat[i];
     const double x0 = (x - sb * (double)e) / sa;
     const double den = c_out * x0 + c_skip * x;
     const float nv = last ? (float)den : (float)(sap * den + sbp * (double)noise[i]);
     lat[i] = nv;
-    if (lat_pair) {
-      lat_pair[(img * 2 + 0) * L + j] = nv;
-      lat_pair[(img * 2 + 1) * L + j] = nv;
+    if (lat_next) {
+      if (next_pairs) {
+        lat_next[(img * 2 + 0) * L + j] = nv;
+        lat_next[(img * 2 + 1) * L + j] = nv;
+      } else {
+        lat_next[i] = nv;
+      }
     }
   }
 }
@@ -228,7 +269,8 @@ cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int
                         const float* bias, int N, int act_in, int act_out, float* y, int ldy, cudaStream_t s) {
   if (M <= 0 || K <= 0 || K > kGemvMaxK || K % 8) return cudaErrorInvalidValue;
   if ((w8 != nullptr) == (w != nullptr) || (w8 && !ws)) return cudaErrorInvalidValue;
-  const int blocks = (N + 7) / 8;
+  const int rows_per_block = 8 * kGemvRows;
+  const int blocks = (N + rows_per_block - 1) / rows_per_block;
   for (int m0 = 0; m0 < M; m0 += kGemvMaxM) {  // rows in chunks of kGemvMaxM
     const int mc = M - m0 < kGemvMaxM ? M - m0 : kGemvMaxM;
     cudaError_t e;
@@ -281,12 +323,13 @@ cudaError_t launch_f32_to_f16(const float* x, size_t n, __half* y, cudaStream_t 
   return launch_kernel(f32_to_f16_kernel, dim3(grid_for(n)), dim3(256), 0, s, 0, x, n, y);
 }
 
-cudaError_t launch_cfg_lcm(const float* eps2, float* latents, const float* noise, int n_img, int L, float cfg,
-                           double c_skip, double c_out, double sa, double sb, double sap, double sbp, int last,
-                           float* lat_pair, cudaStream_t s) {
+cudaError_t launch_cfg_lcm(const float* eps, int eps_pairs, float* latents, const float* noise, int n_img, int L,
+                           float cfg, double c_skip, double c_out, double sa, double sb, double sap, double sbp,
+                           int last, float* lat_next, int next_pairs, cudaStream_t s) {
+  if (n_img <= 0 || L <= 0 || (!last && !noise)) return cudaErrorInvalidValue;
   const size_t total = (size_t)n_img * L;
-  return launch_kernel(cfg_lcm_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, eps2, latents, noise, n_img, L, cfg,
-                       c_skip, c_out, sa, sb, sap, sbp, last, lat_pair);
+  return launch_kernel(cfg_lcm_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, eps, eps_pairs, latents, noise, n_img,
+                       L, cfg, c_skip, c_out, sa, sb, sap, sbp, last, lat_next, next_pairs);
 }
 
 }  // namespace sdg

@@ -106,11 +106,14 @@ cudaError_t launch_concat(const __half* a, int Ca, const __half* b, int Cb, int 
 cudaError_t launch_add(const __half* a, const __half* b, size_t n, __half* y, cudaStream_t s);
 cudaError_t launch_f32_to_f16(const float* x, size_t n, __half* y, cudaStream_t s);
 // Fused CFG combine + LCM step over n_img images of L latent elements.
-// eps2 [n_img, 2, L] (cond, uncond), latents [n_img, L] updated in place,
-// lat_pair [n_img, 2, L] (optional) receives the new latents twice.
-cudaError_t launch_cfg_lcm(const float* eps2, float* latents, const float* noise, int n_img, int L, float cfg,
-                           double c_skip, double c_out, double sqrt_alpha, double sqrt_beta, double sqrt_alpha_prev,
-                           double sqrt_beta_prev, int last, float* lat_pair, cudaStream_t s);
+// eps: [n_img, 2, L] (cond, uncond) when eps_pairs (combined with cfg), else
+// [n_img, L] (cond only). latents [n_img, L] are updated in place; lat_next
+// (optional) receives the new latents laid out for the next forward: twice
+// per image when next_pairs, else once.
+cudaError_t launch_cfg_lcm(const float* eps, int eps_pairs, float* latents, const float* noise, int n_img, int L,
+                           float cfg, double c_skip, double c_out, double sqrt_alpha, double sqrt_beta,
+                           double sqrt_alpha_prev, double sqrt_beta_prev, int last, float* lat_next, int next_pairs,
+                           cudaStream_t s);
 
 int num_sms();
 

@@ -62,7 +62,8 @@ def build_ops(sdg, dev):
         gm = torch.ones(C, device=dev)
         bt = torch.zeros(C, device=dev)
         yg = torch.empty_like(xg)
-        st = torch.empty(B * 32 * 2, dtype=torch.float32, device=dev)
+        st = torch.empty(sdg.lib().sdg_groupnorm_scratch_bytes(B, H * H, C, 32) // 4 + 1, dtype=torch.float32,
+                         device=dev)
         ops[f"gn_silu_{C}_{H}"] = (lambda xg=xg, gm=gm, bt=bt, yg=yg, st=st: sdg.groupnorm(xg, gm, bt, 1e-5, True, out=yg,
                                                                                         stats=st),
                                    0.0, 2.0 * 2 * B * H * H * C)

@@ -85,3 +85,24 @@ def test_lcm_step_identity_cases():
     den = c_out / math.sqrt(a) + c_skip
     a_prev = s.alphas_cumprod[s.timesteps[1]]
     assert np.allclose(out, math.sqrt(a_prev) * den, rtol=1e-6)
+
+
+def test_cfg_only_first_steps_call_pattern():
+    # TpuUnetPipeline.kt:97-104: steps idx < cfg_steps run [cond, uncond] pairs, later steps cond only
+    calls = []
+
+    def fake_unet(lat, t, ctx):
+        calls.append((lat.shape[0], float(ctx[0, 0, 0])))
+        return np.full_like(lat, 0.01)
+
+    n, steps = 3, 4
+    lat = np.zeros((n, 4, 8, 8), np.float32)
+    cond = np.ones((n, 77, 768), np.float32)
+    unc = -np.ones((n, 77, 768), np.float32)
+    noise = np.zeros((steps - 1, n, 4, 8, 8), np.float32)
+    lcm.cfg_denoise(fake_unet, lat, cond, unc, noise, steps=steps, cfg=1.5, cfg_steps=2)
+    assert [c[0] for c in calls] == [2 * n, 2 * n, n, n]
+    assert calls[2][1] == 1.0                       # cond-only steps see the cond context
+    calls.clear()
+    lcm.cfg_denoise(fake_unet, lat, cond, None, noise, steps=steps, cfg=1.0, cfg_steps=4)
+    assert [c[0] for c in calls] == [n] * steps     # cfg <= 1: no guidance at all

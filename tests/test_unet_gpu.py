@@ -158,6 +158,35 @@ def test_lcm_denoise_matches_oracle_loop(engine, unet_weights):
     assert err < 1e-2
 
 
+@pytest.mark.parametrize("cfg_steps,cfg", [(2, 1.5), (0, 1.5), (4, 1.0)])
+def test_lcm_cfg_only_first_steps_matches_oracle(engine, unet_weights, cfg_steps, cfg):
+    # TpuUnetPipeline.kt:75-112: guidance on the first cfg_steps steps, cond-only forwards after them
+    n, H, steps = 2, 16, 4
+    g = torch.Generator().manual_seed(91 + cfg_steps)
+    lat0 = torch.randn((n, 4, H, H), generator=g).numpy()
+    cond = torch.nn.functional.layer_norm(torch.randn((n, 77, 768), generator=g), (768,)).numpy()
+    unc = torch.nn.functional.layer_norm(torch.randn((n, 77, 768), generator=g), (768,)).numpy()
+    noise = torch.randn((steps - 1, n, 4, H, H), generator=g).numpy()
+    got = engine.lcm_denoise(lat0, cond, unc, noise, steps=steps, cfg=cfg, cfg_steps=cfg_steps)
+    ref = LCM.cfg_denoise(lambda l, t, c: oracle_forward(unet_weights, l, np.full((l.shape[0],), t, np.float32), c),
+                          lat0, cond, unc, noise, steps=steps, cfg=cfg, cfg_steps=cfg_steps)
+    err = rel(got, ref)
+    print(f"LCM cfg_steps={cfg_steps} cfg={cfg}: relErr {err:.3e}")
+    assert err < 1e-2
+
+
+def test_cached_context_graph_matches_full_forward(engine):
+    # a denoise call leaves the pair plan's cross-attention K/V cached; a plain forward with another
+    # context afterwards must recompute them (full graph), and agree with a fresh evaluation
+    lat, t, ctx = W.make_inputs(2, 16, 16, seed=21)
+    before = engine.forward(lat.numpy(), t.numpy(), ctx.numpy())
+    g = torch.Generator().manual_seed(5)
+    other = torch.nn.functional.layer_norm(torch.randn((1, 77, 768), generator=g), (768,)).numpy()
+    engine.lcm_denoise(lat.numpy()[:1], other, other, np.zeros((3, 1, 4, 16, 16), np.float32), steps=4, cfg=1.5)
+    after = engine.forward(lat.numpy(), t.numpy(), ctx.numpy())
+    assert np.array_equal(before, after)
+
+
 def test_bad_shape_and_missing_weight_are_reported(sdg, cuda, engine):
     lat = np.zeros((1, 4, 12, 12), np.float32)
     with pytest.raises(sdg.SdgError) as ei:
