@@ -35,6 +35,11 @@ METRIC = "UNet fwd/s (B=2 CFG, 64×64 latent) at 1/2/4/8 B200; % dense-fp16 tens
 UNIT = "fwd/s"
 B, H, W = 2, 64, 64
 FLOPS_PER_FWD = 1.606e12          # algorithmic FLOPs per B=2 64x64 forward (direct-conv count)
+# DRAM bytes (read + write) of one conv3x3 launch at 64x64x320, B=2, from one ncu capture
+# (--set full capture of opbench's conv3x3_320_64); algorithmic bytes of that launch: 12.3 MB
+CONV_TRAFFIC_PER_LAUNCH = 12.80e6
+CONV_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 64x64x320 conv3x3 launch "
+                     "(the most frequent conv3x3 shape), bytes per launch")
 L2_FLUSH_BYTES = 256 << 20        # > 126 MB L2
 
 
@@ -259,17 +264,22 @@ def main():
     h2d = n_lat.nbytes + n_ctx.nbytes + n_t.nbytes
     d2h = out_host.nbytes
 
-    # ---- roofline of the dominant kernel (tcgen05 GEMM / implicit conv), per-launch CUDA events
+    # ---- roofline of the dominant kernel: gemm_tc_kernel's 3x3 implicit-GEMM launches (CONV3), timed per
+    # launch with CUDA events in a graph replay of the forward (sdg_profile); algorithmic FLOPs per launch
     prof = eng.profile(B, H, W)
+    conv_ms, conv_n, conv_fl = prof["CONV3"][0], prof["CONV3"][1], prof["CONV3"][2]
     gemm_ms = sum(prof[c][0] for c in ("CONV3", "GEMM") if c in prof)
     gemm_fl = sum(prof[c][2] for c in ("CONV3", "GEMM") if c in prof)
     gemm_n = sum(prof[c][1] for c in ("CONV3", "GEMM") if c in prof)
     hbm, tc_burst, tc_sust, src = peaks()
-    achieved = gemm_fl / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
-    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel (conv3x3 implicit GEMM + linears)",
+    achieved = conv_fl / (conv_ms / 1000.0) / 1e12 if conv_ms > 0 else None
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel, conv3x3 implicit-GEMM launches",
                 "achieved": achieved, "peak": tc_burst, "unit": "TFLOP/s",
                 "frac": (achieved / tc_burst) if achieved else None, "peak_source": f"{src} bf16_tflops (burst)",
-                "traffic": None, "launches_per_fwd": gemm_n, "flops_per_fwd": gemm_fl,
+                "traffic": CONV_TRAFFIC_PER_LAUNCH, "traffic_note": CONV_TRAFFIC_NOTE,
+                "launches_per_fwd": conv_n, "flops_per_launch": conv_fl / max(conv_n, 1),
+                "all_gemm_tflops": gemm_fl / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None,
+                "all_gemm_launches_per_fwd": gemm_n,
                 "whole_forward_tflops": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12,
                 "whole_forward_frac_of_sustained": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_sust,
                 "categories_ms": {k: round(v[0], 4) for k, v in prof.items()}}

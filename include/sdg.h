@@ -138,9 +138,12 @@ SDG_API int sdg_lcm_denoise_ex(sdg_engine* e, const float* latents, const float*
                                const float* step_noise, int n_img, int H, int W, int steps, float cfg, int cfg_steps,
                                float* out);
 
-/* Per-category device times of one eager forward (replaces
- * Java_..._unetProfile, vk_engine.cpp:854-872, which only logs). Returns the
- * number of rows written (<= cap) or a negative status. */
+/* Per-category device times of one forward (replaces Java_..._unetProfile,
+ * vk_engine.cpp:854-872, which only logs): the forward is captured with a
+ * timing event on each side of every launch and replayed as a graph; each
+ * launch's time is its event interval (launches serialised against their
+ * neighbours). Returns the number of rows written (<= cap) or a negative
+ * status. */
 SDG_API int sdg_profile(sdg_engine* e, int B, int H, int W, sdg_profile_row* rows, int cap);
 
 /* Number of kernel launches of one forward at (B,H,W) (after a forward ran). */
