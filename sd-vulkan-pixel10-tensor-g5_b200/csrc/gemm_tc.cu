@@ -580,16 +580,27 @@ struct TileChoice {
   bool pair = false;  // 256-row tiles on a CTA pair (cta_group::2)
 };
 
-// Cost model (cycles of the slowest CTA): per 64-deep k-block a CTA needs
-// max(MMA cycles, operand bytes it loads / ~64 B per cycle of L2 bandwidth);
-// waves of units over the SMs (CTA pairs: 256-row units over half as many
-// teams, each CTA loading 128 A rows and half the W rows); plus the split-K
-// reduce traffic.
+// Cost model, fitted to launch times measured on B200 over the SD1.5 UNet's GEMM and conv shapes
+// (graph replay, 1-CTA and CTA-pair tiles of width 64..256, 1..32 K splits; median error 5 %):
+//   t = waves * (k-blocks per unit * t_kb + t_unit) + (splits > 1 ? 5.8 us + 0.213 us per MB of partials : 0)
+// A 64-deep k-block costs ~0.33-0.39 us per CTA at every tile width (the tensor pipe does not get
+// cheaper per instruction for narrow tiles), so wider tiles win until they leave SMs idle; t_unit
+// (pipeline fill + epilogue) grows with the tile width.
+struct TileCost {
+  int bn;
+  bool pair;
+  double us_per_kb, us_per_unit;
+};
+constexpr TileCost kTileCosts[] = {
+    {256, false, 0.323, 6.09}, {192, false, 0.393, 3.89}, {160, false, 0.353, 3.52}, {128, false, 0.355, 2.90},
+    {64, false, 0.341, 1.27},  {256, true, 0.323, 7.15},  {192, true, 0.382, 4.36},  {160, true, 0.353, 3.75},
+    {128, true, 0.347, 3.20},
+};
+
 TileChoice choose_tiles(const GemmArgs& a) {
   TileChoice best;
   const int KB = a.K / BK;
   const int sms = num_sms();
-  const int num_m = (a.M + BM - 1) / BM;
   best.kb_per_split = KB;
   if (a.bn) {
     best.bn = a.bn;
@@ -599,38 +610,30 @@ TileChoice choose_tiles(const GemmArgs& a) {
     best.bn = 16;
     return best;
   }
-  const bool pair_ok = a.w8 == nullptr && a.M > BM;
-  if (a.epi == kEpiGeglu) {
-    best.bn = 256;
-    best.pair = pair_ok;
-    return best;
-  }
-  const int cands[4] = {256, 160, 128, 64};
+  const bool w8 = a.w8 != nullptr;
+  const bool pair_ok = !w8 && a.M > BM;
   double best_t = 1e30;
-  for (int pr = 0; pr < 2; ++pr) {
-    if (pr && !pair_ok) continue;
-    for (int bn : cands) {
-      if (a.N % bn != 0 || (pr && bn == 64)) continue;
-      const int tiles = (pr ? (a.M + 2 * BM - 1) / (2 * BM) : num_m) * (a.N / bn);
-      const int teams = pr ? sms / 2 : sms;
-      const double wrows = pr ? bn / 2 : bn;
-      const double kcost = std::max(2.0 * bn, (kATileBytes + wrows * BK * 2.0) / 64.0);
-      const int max_split = (a.epi == kEpiNchwF32) ? 1 : std::max(1, std::min(32, KB / 6));
-      for (int sp = 1; sp <= max_split; ++sp) {
-        const int kbs = (KB + sp - 1) / sp;
-        const int real_sp = (KB + kbs - 1) / kbs;
-        if (real_sp != sp) continue;
-        const int units = tiles * sp;
-        const int waves = (units + teams - 1) / teams;
-        double t = (double)waves * (kbs * kcost + 600.0);  // + per-unit pipeline fill / epilogue
-        if (sp > 1) t += ((double)sp * a.M * a.N * 4.0 + a.M * a.N * 2.0) / 2500.0 + 3000.0;  // reduce pass
-        if (t < best_t * 0.97) {
-          best_t = t;
-          best.bn = bn;
-          best.splits = sp;
-          best.kb_per_split = kbs;
-          best.pair = pr != 0;
-        }
+  for (const TileCost& tcst : kTileCosts) {
+    const int bn = tcst.bn;
+    if (a.N % bn != 0 || (tcst.pair && !pair_ok)) continue;
+    if (w8 && bn == 192) continue;                  // wo8 tiles: 64 / 128 / 160 / 256
+    if (a.epi == kEpiGeglu && bn != 256) continue;  // value/gate halves live in one 256-wide tile
+    const int tiles = (tcst.pair ? (a.M + 2 * BM - 1) / (2 * BM) : (a.M + BM - 1) / BM) * (a.N / bn);
+    const int teams = tcst.pair ? sms / 2 : sms;
+    const int max_split = (a.epi == kEpiNchwF32 || a.epi == kEpiGeglu) ? 1 : std::max(1, std::min(32, KB / 3));
+    for (int sp = 1; sp <= max_split; ++sp) {
+      const int kbs = (KB + sp - 1) / sp;
+      const int real_sp = (KB + kbs - 1) / kbs;
+      if (real_sp != sp) continue;
+      const int waves = (tiles * sp + teams - 1) / teams;
+      double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit);
+      if (sp > 1) t += 5.8 + 0.213 * ((double)sp * a.M * a.N * 4.0 / 1e6);
+      if (t < best_t) {
+        best_t = t;
+        best.bn = bn;
+        best.splits = sp;
+        best.kb_per_split = kbs;
+        best.pair = tcst.pair;
       }
     }
   }
@@ -742,6 +745,7 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   if (!make_tmap_2d(&mw, a.w, a.N, a.K, a.K, tc.pair ? bn / 2 : bn, BK)) return cudaErrorInvalidValue;
   if (tc.pair) {
     switch (bn) {
+      case 192: return launch_bn<192, false, true>(d, ma0, ma1, mw, s);
       case 128: return launch_bn<128, false, true>(d, ma0, ma1, mw, s);
       case 160: return launch_bn<160, false, true>(d, ma0, ma1, mw, s);
       case 256: return launch_bn<256, false, true>(d, ma0, ma1, mw, s);
@@ -749,6 +753,7 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
     }
   }
   switch (bn) {
+    case 192: return launch_bn<192, false, false>(d, ma0, ma1, mw, s);
     case 16: return launch_bn<16, false, false>(d, ma0, ma1, mw, s);
     case 64: return launch_bn<64, false, false>(d, ma0, ma1, mw, s);
     case 128: return launch_bn<128, false, false>(d, ma0, ma1, mw, s);
