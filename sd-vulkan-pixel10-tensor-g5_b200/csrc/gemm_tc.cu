@@ -108,6 +108,20 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Pull the lines the epilogue will read for columns [n, n+CH) of row m into L1 ahead of use.
+template <int CH>
+__device__ __forceinline__ void epi_prefetch(const GemmDev& p, int m, int img, int n, bool mvalid) {
+  if (n >= p.N) return;
+  if (p.bias) prefetch_l1(p.bias + n);
+  if (p.rowbias && mvalid) prefetch_l1(p.rowbias + (size_t)img * p.rowbias_ld + n);
+  if (p.residual && mvalid) prefetch_l1(p.residual + (size_t)m * p.ld_res + n);
+  (void)CH;
+}
+
 __device__ __forceinline__ void add8_f32(const float* src, float (&v)[8]) {  // src 16-byte aligned
   const float4 a = __ldg(reinterpret_cast<const float4*>(src));
   const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
@@ -416,13 +430,14 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       int m_blk, n_blk, kb0, kb1;
       decode(unit, m_blk, n_blk, kb0, kb1);
       const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
-      bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
       const int m = m_blk * TM + (int)rank * BM + row;
       const int img = m / p.rows_per_image;
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
+      if (p.splits == 1 && p.epi != kEpiGeglu) epi_prefetch<C::kChunk>(p, m, img, n0 + eh * C::kChunk, mvalid);
+      bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
       constexpr int CH = C::kChunk;
       if (p.epi == kEpiGeglu) {
@@ -430,6 +445,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         const int nout0 = n_blk * HALF;
 #pragma unroll 1
         for (int c = eh * CH; c < HALF; c += kSplit * CH) {
+          if (p.bias && c + kSplit * CH < HALF) {
+            prefetch_l1(p.bias + n0 + c + kSplit * CH);
+            prefetch_l1(p.bias + n0 + HALF + c + kSplit * CH);
+          }
           uint32_t ra[32], rg[32];
           if constexpr (CH == 32) {
             tmem_ld32(t_row + c, ra);
@@ -466,6 +485,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       } else {
 #pragma unroll 1
         for (int c = eh * CH; c < BN; c += kSplit * CH) {
+          if (p.splits == 1) epi_prefetch<CH>(p, m, img, n0 + c + kSplit * CH, mvalid);  // next chunk's lines
           uint32_t r[32];
           if constexpr (CH == 32) {
             tmem_ld32(t_row + c, r);
