@@ -113,7 +113,11 @@ struct Engine;
 
 class Builder {
  public:
-  Builder(Engine& e, Plan& pl, bool dry, cudaStream_t s) : e_(e), pl_(pl), dry_(dry), s_(s) {}
+  Builder(Engine& e, Plan& pl, bool dry, cudaStream_t s, cudaStream_t side = nullptr)
+      : e_(e), pl_(pl), dry_(dry), s_(s), s2_(side) {}
+  ~Builder() {
+    for (cudaEvent_t ev : evs_) cudaEventDestroy(ev);
+  }
   int run();  // issues the whole forward; returns SDG status
   size_t peak() const { return peak_; }
   int launches() const { return launches_; }
@@ -134,6 +138,41 @@ class Builder {
   int launches_ = 0;
   int status_ = SDG_OK;
   int gn_slot_ = 0;
+  // Side stream: work that depends only on data already issued on s_ runs there concurrently
+  // (fork: event on s_ -> side waits; join: event on side -> s_ waits). Its GEMMs take no split-K
+  // workspace (the arena's scope scratch is reused by the main stream). Not used when profiling.
+  cudaStream_t s2_ = nullptr;
+  bool on_side_ = false;
+  std::vector<cudaEvent_t> evs_;
+  std::vector<cudaEvent_t> kv_ready_;  // per transformer: its context K/V are written
+  cudaEvent_t new_event() {
+    cudaEvent_t ev = nullptr;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    evs_.push_back(ev);
+    return ev;
+  }
+  template <typename F>
+  cudaEvent_t on_side(F&& f) {
+    if (!s2_ || dry_ || profile || !ok()) {
+      f();
+      return nullptr;
+    }
+    cudaEvent_t fork = new_event();
+    cudaEventRecord(fork, s_);
+    cudaStreamWaitEvent(s2_, fork, 0);
+    std::swap(s_, s2_);
+    on_side_ = true;
+    f();
+    on_side_ = false;
+    std::swap(s_, s2_);
+    cudaEvent_t done = new_event();
+    cudaEventRecord(done, s2_);
+    return done;
+  }
+  void join(cudaEvent_t ev) {
+    if (ev) cudaStreamWaitEvent(s_, ev, 0);
+  }
+  void ctx_kv(const TfW& t, const CrossBufs& cb);
   std::map<long, AttnBufs> attn_;
   std::vector<CrossBufs> cross_;
   int cross_idx_ = 0;
@@ -167,6 +206,7 @@ class Builder {
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
+  cudaStream_t stream2 = nullptr;  // side stream for independent work inside a forward (fork/join)
   std::unordered_map<std::string, HostWeight> host;
   bool prepared = false;
   bool wo8 = false;  // weight-only int8 (set by sdg_quantize_wo8 before preparation)
@@ -531,7 +571,7 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
 void Builder::gemm(GemmArgs a, int cat) {
   cat_flops[cat] += 2.0 * a.M * a.N * a.K;
   const size_t mark = off_;  // split-K workspace lives only until the GEMM's reduce pass
-  a.ws_bytes = gemm_workspace_bytes(a);
+  a.ws_bytes = on_side_ ? 0 : gemm_workspace_bytes(a);
   a.ws = a.ws_bytes ? alloc_f(a.ws_bytes / 4) : nullptr;
   if (dry_ || !ok()) {
     launches_ += a.ws_bytes ? 2 : 1;
@@ -560,6 +600,22 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
   const int B = pl_.B, HW = H * W, M = B * HW;
   Buf out{alloc_h((size_t)M * r.cout), r.cout};
   const size_t mark = off_;
+  // 1x1 shortcut (channel change): needs only the block input, so it runs on the side stream
+  // while GroupNorm / conv1 / GroupNorm run here; conv2 joins it (residual)
+  const __half* resid = x.p;
+  cudaEvent_t sc_done = nullptr;
+  if (r.has_sc) {
+    __half* sc = alloc_h((size_t)M * r.cout);
+    sc_done = on_side([&] {
+      GemmArgs a;
+      a.M = M; a.N = r.cout; a.K = x.C + (x2 ? x2->C : 0); a.taps = 1;
+      a.a0 = x.p; a.cin0 = x.C;
+      if (x2) { a.a1 = x2->p; a.cin1 = x2->C; }
+      set_w(a, r.sc.w, r.sc.w8, r.sc.ws); a.bias = r.sc.b; a.out = sc;
+      gemm(a, kCatGemm);
+    });
+    resid = sc;
+  }
   __half* h = alloc_h((size_t)M * r.cin);
   gn(x, x2, B, HW, r.n1, kResEps, true, h);
   __half* h2 = alloc_h((size_t)M * r.cout);
@@ -574,17 +630,7 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
   }
   __half* h3 = alloc_h((size_t)M * r.cout);
   gn(Buf{h2, r.cout}, nullptr, B, HW, r.n2, kResEps, true, h3);
-  const __half* resid = x.p;
-  if (r.has_sc) {
-    __half* sc = alloc_h((size_t)M * r.cout);
-    GemmArgs a;
-    a.M = M; a.N = r.cout; a.K = x.C + (x2 ? x2->C : 0); a.taps = 1;
-    a.a0 = x.p; a.cin0 = x.C;
-    if (x2) { a.a1 = x2->p; a.cin1 = x2->C; }
-    set_w(a, r.sc.w, r.sc.w8, r.sc.ws); a.bias = r.sc.b; a.out = sc;
-    gemm(a, kCatGemm);
-    resid = sc;
-  }
+  join(sc_done);
   {
     GemmArgs a;
     a.M = M; a.N = r.cout; a.K = 9 * r.cout; a.taps = 9;
@@ -596,11 +642,26 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
   return out;
 }
 
+// Cross-attention K and V^T of one transformer from the context: [B*77, 768] x [768, 2C]
+// scattered into the padded per-head layouts.
+void Builder::ctx_kv(const TfW& t, const CrossBufs& cb) {
+  const int C = t.C, d = C / kHeads, dp = (d + 63) / 64 * 64, d16 = (d + 15) / 16 * 16;
+  GemmArgs a;
+  a.M = pl_.B * kCtxLen; a.N = t.kv2.N; a.K = kCtxDim; a.a0 = ctx16_; a.cin0 = kCtxDim;
+  set_w(a, t.kv2.w, t.kv2.w8, t.kv2.ws); a.bias = t.kv2.b;
+  a.epi = kEpiHeads; a.rows_per_image = kCtxLen;
+  a.head_out[0] = cb.k; a.head_out[1] = cb.vt; a.head_out[2] = nullptr;
+  a.head_C = C; a.heads = kHeads; a.head_d = d; a.head_dp = dp;
+  a.head_vt = 1; a.head_d16 = d16; a.head_spad = kCtxPad;
+  gemm(a, kCatGemm);
+}
+
 Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   const int B = pl_.B, S = H * W, M = B * S, C = t.C;
   const int d = C / kHeads, dp = (d + 63) / 64 * 64, d16 = (d + 15) / 16 * 16;
   AttnBufs& ab = level_bufs(C, S);
-  CrossBufs& cb = cross_[cross_idx_++];
+  const int ci = cross_idx_++;
+  CrossBufs& cb = cross_[ci];
   Buf out{alloc_h((size_t)M * C), C};
   const size_t mark = off_;
   __half* g = alloc_h((size_t)M * C);
@@ -648,8 +709,12 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
   ln(tt, t.ln2);
   heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
-  if (!ctx_cached)
-    heads(ctx16_, B * kCtxLen, kCtxDim, t.kv2, kCtxLen, cb.k, cb.vt, nullptr, 1, kCtxPad);  // K, V^T from context
+  if (!ctx_cached) {  // K, V^T from the context: issued on the side stream at the start of the forward
+    if (ci < (int)kv_ready_.size())
+      join(kv_ready_[ci]);
+    else
+      ctx_kv(t, cb);
+  }
   attn(ab.q, cb.k, cb.vt, kCtxLen, kCtxPad);                       // cross-attention
   lin(o, C, t.out2, tt, tt);
   ln(tt, t.ln3);
@@ -752,6 +817,19 @@ int Builder::run() {
   } else {
     launches_ += 3 + 3 * ((B + 7) / 8);
   }
+  if (!ctx_cached) {
+    // every transformer's context K/V, in graph order, on the side stream (one event each)
+    std::vector<const TfW*> tfs;
+    for (int i = 0; i < 3; ++i)
+      for (int r = 0; r < 2; ++r) tfs.push_back(&w.down_tf[i][r]);
+    tfs.push_back(&w.mid_tf);
+    for (int i = 1; i < 4; ++i)
+      for (int r = 0; r < 3; ++r) tfs.push_back(&w.up_tf[i][r]);
+    for (size_t i = 0; i < tfs.size(); ++i) {
+      cudaEvent_t ev = on_side([&] { ctx_kv(*tfs[i], cross_[i]); });
+      kv_ready_.push_back(ev);  // null when run inline (dry / profiling): nothing to join
+    }
+  }
   // conv_in
   Buf x{alloc_h((size_t)M * 320), 320};
   {
@@ -824,6 +902,7 @@ Engine::~Engine() {
   if (warena) cudaFree(warena);
   if (op_err) cudaFree(op_err);
   if (stream) cudaStreamDestroy(stream);
+  if (stream2) cudaStreamDestroy(stream2);
 }
 
 int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
@@ -846,7 +925,7 @@ int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
   SDG_CUDA_TRY(cudaMemset(pl->arena, 0, pl->arena_bytes));
   // eager validation pass (sets kernel attributes, surfaces argument errors)
   {
-    Builder b(*this, *pl, false, stream);
+    Builder b(*this, *pl, false, stream, stream2);
     st = b.run();
     if (st) { cudaFree(pl->arena); return st; }
     pl->launches = b.launches();
@@ -854,7 +933,7 @@ int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
   }
   SDG_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   {
-    Builder b(*this, *pl, false, stream);
+    Builder b(*this, *pl, false, stream, stream2);
     st = b.run();
     cudaGraph_t g = nullptr;
     cudaError_t ce = cudaStreamEndCapture(stream, &g);
@@ -865,7 +944,7 @@ int Engine::get_plan(int B, int H, int W, int mode, Plan** out) {
   SDG_CUDA_TRY(cudaGraphInstantiate(&pl->exec, pl->graph, 0));
   SDG_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
   {
-    Builder b(*this, *pl, false, stream);
+    Builder b(*this, *pl, false, stream, stream2);
     b.ctx_cached = true;
     st = b.run();
     cudaGraph_t g = nullptr;
@@ -979,6 +1058,7 @@ SDG_API int sdg_init(int device, const char* weights_dir, sdg_engine** out) {
   auto* h = new sdg_engine();
   h->e.device = device;
   if (cudaStreamCreateWithFlags(&h->e.stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&h->e.stream2, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&h->e.op_err, 256) != cudaSuccess || cudaMemset(h->e.op_err, 0, 256) != cudaSuccess) {
     delete h;
     return fail(SDG_ERR_CUDA, "stream / error word allocation failed");
