@@ -145,6 +145,7 @@ class Builder {
   bool on_side_ = false;
   std::vector<cudaEvent_t> evs_;
   std::vector<cudaEvent_t> kv_ready_;  // per transformer: its context K/V are written
+  cudaEvent_t temb_ready_ = nullptr;    // time-embedding projections written (joined once)
   cudaEvent_t new_event() {
     cudaEvent_t ev = nullptr;
     cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
@@ -625,6 +626,8 @@ Buf Builder::resnet(const ResW& r, const Buf& x, const Buf* x2, int H, int W) {
     a.a0 = h; a.cin0 = r.cin; a.B = B; a.H = H; a.W = W;
     set_w(a, r.c1.w, r.c1.w8, r.c1.ws); a.bias = r.c1.b;
     a.rowbias = tp_all_ ? tp_all_ + r.tp_off : nullptr; a.rowbias_ld = e_.w.tp_N; a.rows_per_image = HW;
+    join(temb_ready_);
+    temb_ready_ = nullptr;
     a.out = h2;
     gemm(a, kCatConv3);
   }
@@ -797,7 +800,7 @@ int Builder::run() {
   const size_t persistent_end = off_;
   (void)persistent_end;
 
-  if (!dry_) {
+  if (!dry_) temb_ready_ = on_side([&] {  // time embedding + projections: needed first by the first conv1
     begin_op(kCatMisc);
     check(launch_time_embedding(pl_.t_in, B, B, pl_.mode == 1 ? pl_.tproj_in : nullptr, te, s_), "time_embedding", kCatMisc);
     begin_op(kCatGemv);
@@ -814,9 +817,9 @@ int Builder::run() {
       begin_op(kCatMisc);
       check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
     }
-  } else {
+  });
+  else
     launches_ += 3 + 3 * ((B + 7) / 8);
-  }
   if (!ctx_cached) {
     // every transformer's context K/V, in graph order, on the side stream (one event each)
     std::vector<const TfW*> tfs;
