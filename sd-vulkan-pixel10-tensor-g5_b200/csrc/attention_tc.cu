@@ -35,7 +35,7 @@ struct AttnCfg {
   static constexpr bool ONES = ONES_;
   static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
   static constexpr int NKATOM = BKV / 64;                     // 128B swizzle atoms along keys
-  static constexpr int NKV = (DP == 64) ? (NQT >= 4 ? 2 : 4) : (DP == 128 ? 3 : 2);  // K/V pipeline depth
+  static constexpr int NKV = (DP == 64 && BKV == 64) ? (NQT >= 4 ? 2 : 4) : (DP == 128 ? 3 : 2);  // K/V pipeline depth
   static constexpr uint32_t kQTile = 128 * 128 * NATOM;       // bytes per 128-row Q tile
   static constexpr uint32_t kKTile = BKV * 128 * NATOM;       // bytes of K per stage
   static constexpr uint32_t kVAtom = D16 * 128;               // bytes of one 64-key V^T atom
@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     // raised when a new score exceeds it by more than 2^8 (then that O row and l
     // are rescaled through tcgen05.ld/st), so P <= 256 always fits fp16 and the
     // per-tile path is: load S, max, exp2, store P.
-    static_assert(BKV == 64, "softmax path is written for 64-key tiles");
+    static_assert(BKV % 64 == 0, "softmax path works on whole 64-key swizzle atoms");
+    constexpr int NCH = BKV / 32;   // 32-key chunks of a score row
     constexpr float kRescale = 8.f;
     const int sw = warp - 2;        // 0 .. 4*NQT-1
     const int t = sw >> 2;          // query tile of this warpgroup
@@ -268,9 +269,9 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sa[32], sb[32];
-      tmem_ld32(t_s, sa);
-      tmem_ld32(t_s + 32, sb);
+      uint32_t sv[NCH][32];
+#pragma unroll
+      for (int h = 0; h < NCH; ++h) tmem_ld32(t_s + 32 * h, sv[h]);
       tmem_wait_ld();
       // S is in registers: release its TMEM so QK^T of the next tile can start
       tc_fence_before();
@@ -279,14 +280,16 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       const int kbase = j * BKV;
       if (kbase + BKV > p.Sk) {  // ragged last tile: masked keys score -inf (exp2 -> 0)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (kbase + e >= p.Sk) sa[e] = __float_as_uint(-INFINITY);
-          if (kbase + 32 + e >= p.Sk) sb[e] = __float_as_uint(-INFINITY);
-        }
+        for (int h = 0; h < NCH; ++h)
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (kbase + 32 * h + e >= p.Sk) sv[h][e] = __float_as_uint(-INFINITY);
       }
       float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fmaxf(__uint_as_float(sa[e]), __uint_as_float(sb[e])));
+      for (int h = 0; h < NCH; ++h)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sv[h][e]));
       const float m_cand = mx * p.sl2;
       const bool need = m_cand > m_used + kRescale;
       const float m_new = need ? m_cand : m_used;
@@ -312,25 +315,28 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
       }
       float rs = 0.f;
+      // P row in 64-key swizzle atoms of 128 rows x 128 B each
       uint8_t* prow = sP + (2 * t + (j & 1)) * CF::kPTile + row * 128;
-      auto emit_half = [&](const uint32_t (&sv)[32], int q0c) {
-        // 32 keys -> four 16-byte chunks (chunk index q0c..q0c+3) of the 128B-swizzled K-major row
+      auto emit_chunk = [&](const uint32_t (&c32)[32], int h) {
+        // keys 32h..32h+31 -> four 16-byte chunks of the 128B-swizzled K-major row of atom h/2
+        uint8_t* arow = prow + (h >> 1) * 16384;
+        const int q0c = (h & 1) * 4;
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float x0 = ex2_approx(fmaf(__uint_as_float(sv[e]), p.sl2, -m_new));
-          const float x1 = ex2_approx(fmaf(__uint_as_float(sv[e + 1]), p.sl2, -m_new));
+          const float x0 = ex2_approx(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new));
           if constexpr (!ONES) rs += x0 + x1;
           pk[e >> 1] = pack_half2(x0, x1);
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(prow + (((q0c + q) ^ r7) << 4)) = u;
+          *reinterpret_cast<uint4*>(arow + (((q0c + q) ^ r7) << 4)) = u;
         }
       };
-      emit_half(sa, 0);
-      emit_half(sb, 4);
+#pragma unroll
+      for (int h = 0; h < NCH; ++h) emit_chunk(sv[h], h);
       if constexpr (!ONES) l = l * corr + rs;
       m_used = m_new;
       fence_proxy_async_smem();
@@ -423,6 +429,7 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
   switch (a.d16) {
     case 48:
       if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
+      if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true>>(a, err, s);  // fewer, wider QK^T MMAs
       return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
     case 80: return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
