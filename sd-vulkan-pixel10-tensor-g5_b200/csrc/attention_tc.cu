@@ -35,7 +35,7 @@ struct AttnCfg {
   static constexpr bool ONES = ONES_;
   static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
   static constexpr int NKATOM = BKV / 64;                     // 128B swizzle atoms along keys
-  static constexpr int NKV = (DP == 64 && BKV == 64) ? (NQT >= 4 ? 2 : 4) : (DP == 128 ? 3 : 2);  // K/V pipeline depth
+  static constexpr int NKV = BKV > 64 ? 2 : (DP == 64 ? (NQT >= 4 ? 2 : 4) : (DP == 128 ? 3 : 2));  // K/V pipeline depth
   static constexpr uint32_t kQTile = 128 * 128 * NATOM;       // bytes per 128-row Q tile
   static constexpr uint32_t kKTile = BKV * 128 * NATOM;       // bytes of K per stage
   static constexpr uint32_t kVAtom = D16 * 128;               // bytes of one 64-key V^T atom
@@ -432,7 +432,9 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
       if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true>>(a, err, s);  // fewer, wider QK^T MMAs
       return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
-    case 80: return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
+    case 80:
+      if (a.Sk >= 512) return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles
+      return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
     case 160: return launch_cfg<AttnCfg<192, 64, 1, 160, false>>(a, err, s);
     default: return cudaErrorInvalidValue;
   }
