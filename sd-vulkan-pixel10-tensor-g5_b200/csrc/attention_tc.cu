@@ -430,11 +430,9 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
     case 48:
       if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
       if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true>>(a, err, s);  // fewer, wider QK^T MMAs
-      return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);
+      return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);  // short key sets (cross-attention)
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
-    case 80:
-      if (a.Sk >= 512) return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles
-      return launch_cfg<AttnCfg<128, 64, 2, 80, false>>(a, err, s);
+    case 80: return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles
     case 160: return launch_cfg<AttnCfg<192, 64, 1, 160, false>>(a, err, s);
     default: return cudaErrorInvalidValue;
   }

@@ -79,7 +79,7 @@ def build_ops(sdg, dev):
     ops["launch_floor_add64"] = (lambda: sdg.add(xt, xt, out=yt), 0.0, 0.0)   # per-launch floor in a graph
     heads = 8                                                               # config 2 attention
     for name, Sq, Sk, d in (("attn_self_4096_d40", 4096, 4096, 40), ("attn_self_1024_d80", 1024, 1024, 80),
-                            ("attn_self_256_d160", 256, 256, 160), ("attn_cross_4096_d40", 4096, 77, 40),
+                            ("attn_self_256_d160", 256, 256, 160), ("attn_cross_4096_d40", 4096, 77, 40), ("attn_cross_1024_d80", 1024, 77, 80),
                             ("attn_cross_256_d160", 256, 77, 160)):
         C = heads * d
         q = sdg.heads_layout(rn(B * Sq, C), B, Sq, heads, d)
