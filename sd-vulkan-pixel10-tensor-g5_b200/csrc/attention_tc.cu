@@ -29,27 +29,56 @@
 namespace sdg {
 namespace {
 
-template <int DP_, int BKV_, int NQT_, int D16_, bool ONES_>
+// TPV: PV computed transposed, O^T[d][q] += V^T[d][keys] * P^T — one M=64 MMA per 16 keys covers
+// both query tiles (N = 256), half the PV instructions of the per-tile form (M=128, N=D16).
+template <int DP_, int BKV_, int NQT_, int D16_, bool ONES_, bool TPV_ = false>
 struct AttnCfg {
   static constexpr int DP = DP_, BKV = BKV_, NQT = NQT_, D16 = D16_;
   static constexpr bool ONES = ONES_;
+  static constexpr bool TPV = TPV_;
+  static_assert(!TPV || (NQT == 2 && BKV == 128 && ONES && D16 <= 64), "transposed PV: two 128-row query tiles");
+  static constexpr int DV = TPV ? 64 : D16;                   // rows of a V^T atom
   static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
   static constexpr int NKATOM = BKV / 64;                     // 128B swizzle atoms along keys
   static constexpr int NKV = BKV > 64 ? 2 : (DP == 64 ? (NQT >= 4 ? 2 : 4) : (DP == 128 ? 3 : 2));  // K/V pipeline depth
   static constexpr uint32_t kQTile = 128 * 128 * NATOM;       // bytes per 128-row Q tile
   static constexpr uint32_t kKTile = BKV * 128 * NATOM;       // bytes of K per stage
-  static constexpr uint32_t kVAtom = D16 * 128;               // bytes of one 64-key V^T atom
+  static constexpr uint32_t kVAtom = DV * 128;                // bytes of one 64-key V^T atom
   static constexpr uint32_t kVTile = NKATOM * kVAtom;         // bytes of V^T per stage
   static constexpr uint32_t kPTile = 128 * BKV * 2;           // fp16 P per query tile
   static constexpr int PVS = (D16 + 31) / 32 * 32;            // TMEM column stride of PV buffers
-  static constexpr int kTmemNeed = NQT * BKV + NQT * PVS;
+  static constexpr int kTmemNeed = NQT * BKV + (TPV ? NQT * 128 : NQT * PVS);
   static constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
   static constexpr int kThreads = 64 + 128 * NQT;
-  static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)2 * NQT * kPTile + 1024;
+  static constexpr size_t kSmem = 1024 + (size_t)NQT * kQTile + (size_t)NKV * (kKTile + kVTile) + (size_t)2 * NQT * kPTile + 1024 +
+                                  (TPV ? 1024 : 0);  // TPV: per-row O^T correction factors
   static_assert(kSmem <= 232448, "attention tile configuration exceeds 227 KB of shared memory");
   static_assert(kTmemNeed <= 512, "attention tile configuration exceeds TMEM");
   static_assert(kVAtom % 1024 == 0, "V^T atoms must stay 1024-byte aligned");
 };
+
+// Named barrier over `n` threads with an AND / OR reduction of a predicate.
+__device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ bool bar_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void bar_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 struct AttnDev {
   int heads, Sq, Sk, d;
@@ -111,7 +140,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   if constexpr (ONES) {
     // rows d..D16-1 of every V^T atom: row d = 1.0 (row-sum column of PV), the rest 0.
     // TMA never writes these rows; the generic-proxy writes are fenced before any MMA.
-    const int extra = D16 - p.d;
+    const int extra = CF::DV - p.d;
     const int per_stage = CF::NKATOM * extra * 8;  // 16-byte chunks
     for (int i = threadIdx.x; i < NKV * per_stage; i += blockDim.x) {
       const int s = i / per_stage, rem = i % per_stage;
@@ -181,6 +210,19 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
         mma_commit(s_full(t));
       };
+      // TPV: both tiles' P_j side by side (rows 0..255 of each 64-key atom) are the B operand
+      auto issue_pv_both = [&](int s, int j) {
+        const uint32_t d_o = tmem + NQT * BKV;
+        constexpr uint32_t idesc_t = idesc_f16(64, NQT * 128, false);
+        const uint8_t* pbuf = sP + (j & 1) * NQT * CF::kPTile;
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const int a = kk >> 2;
+          const uint64_t da = sdesc_sw128(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom) + (kk & 3) * 32, 16, 1024);
+          const uint64_t db = sdesc_sw128(smem_u32(pbuf + a * NQT * 16384) + (kk & 3) * 32, 16, 1024);
+          mma_f16_ss(d_o, da, db, idesc_t, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(pv_full(0, j & 1));
+      };
       auto issue_pv = [&](int t, int s, int j) {
         const uint32_t d_o = tmem + NQT * BKV + t * CF::PVS;
         const uint8_t* pbuf = sP + (2 * t + (j & 1)) * CF::kPTile;
@@ -215,13 +257,26 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
             ++nq[t];
             progress = true;
           }
-          if (np[t] < nq[t] && mbar_test(p_full(t, np[t] & 1), (np[t] >> 1) & 1)) {
+          if constexpr (!CF::TPV) {
+            if (np[t] < nq[t] && mbar_test(p_full(t, np[t] & 1), (np[t] >> 1) & 1)) {
+              tc_fence_after();
+              issue_pv(t, np[t] % NKV, np[t]);
+              ++np[t];
+              progress = true;
+            }
+            min_np = min(min_np, np[t]);
+          }
+        }
+        if constexpr (CF::TPV) {  // np[0] counts the joint PVs
+          const int k = np[0];
+          if (k < nq[0] && k < nq[1] && mbar_test(p_full(0, k & 1), (k >> 1) & 1) &&
+              mbar_test(p_full(1, k & 1), (k >> 1) & 1)) {
             tc_fence_after();
-            issue_pv(t, np[t] % NKV, np[t]);
-            ++np[t];
+            issue_pv_both(k % NKV, k);
+            ++np[0];
             progress = true;
           }
-          min_np = min(min_np, np[t]);
+          min_np = np[0];
         }
         while (kv_released < min_np) {  // every tile's QK and PV of this K/V stage issued
           mma_commit(kv_empty(kv_released % NKV));
@@ -241,6 +296,141 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       }
       mma_commit(drain);
       mbar_wait(drain, 0, p.err, kDevTimeoutDrain);
+    }
+  } else if constexpr (CF::TPV) {
+    // ---------------------------------------------------------------- softmax, transposed PV
+    // As the per-tile path below, but O^T accumulates in TMEM for both tiles: d row r of the
+    // M=64 accumulator sits in lane (r % 16) + 32 (r / 16), query row `row` of tile t in column
+    // 128 t + row. A row-max raise rescales that row's O^T column across all 64 lanes, so the
+    // four warps of a tile decide rescales and aborts together (named-barrier reductions) and
+    // each warp rescales the lanes of its own quadrant.
+    constexpr int NCH = BKV / 32;
+    constexpr float kRescale = 8.f;
+    const int sw = warp - 2;
+    const int t = sw >> 2;
+    const int lg = warp & 3;
+    const int row = lg * 32 + lane;
+    const int bar_id = 1 + t;  // named barrier of this tile's 128 softmax threads
+    const uint32_t lane_off = static_cast<uint32_t>(lg * 32) << 16;
+    const uint32_t t_s = tmem + t * BKV + lane_off;
+    const uint32_t t_ot = tmem + NQT * BKV + t * 128 + lane_off;
+    float* corr_s = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 1024) + t * 128;
+    const int r7 = row & 7;
+    float m_used = -INFINITY;
+    bool ok = true;
+    auto wait_pv = [&](int k) -> bool {  // joint PV(k) complete
+      return mbar_wait(pv_full(0, k & 1), (k >> 1) & 1, p.err, kDevTimeoutAttn);
+    };
+    for (int j = 0; j < nkv; ++j) {
+      bool mine = mbar_wait(s_full(t), j & 1, p.err, kDevTimeoutAttn);
+      mine = __all_sync(0xffffffffu, mine);
+      uint32_t sv[NCH][32];
+      float m_new = m_used, corr = 1.f;
+      bool need = false;
+      if (mine) {
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < NCH; ++h) tmem_ld32(t_s + 32 * h, sv[h]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free(t));
+        const int kbase = j * BKV;
+        if (kbase + BKV > p.Sk) {
+#pragma unroll
+          for (int h = 0; h < NCH; ++h)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (kbase + 32 * h + e >= p.Sk) sv[h][e] = __float_as_uint(-INFINITY);
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < NCH; ++h)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sv[h][e]));
+        const float m_cand = mx * p.sl2;
+        need = m_cand > m_used + kRescale;
+        m_new = need ? m_cand : m_used;
+        corr = need ? ex2_approx(m_used - m_new) : 1.f;
+        corr_s[row] = corr;
+      }
+      if (!bar_and(bar_id, 128, mine)) { ok = false; break; }
+      const bool rescale = bar_or(bar_id, 128, need) && j > 0;
+      // P buffer j%2 was read by PV(j-2); a rescale needs PV(j-1) retired as well
+      bool waited = true;
+      if (rescale || j >= 2) waited = wait_pv(rescale ? j - 1 : j - 2);
+      waited = __all_sync(0xffffffffu, waited);
+      if (waited && rescale) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(t_ot + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr_s[c + e]);
+          tmem_st16(t_ot + c, r);
+        }
+        tmem_wait_st();
+      }
+      if (!bar_and(bar_id, 128, waited)) { ok = false; break; }  // also: every read of corr_s is done
+      uint8_t* prow = sP + (j & 1) * NQT * CF::kPTile + (t * 128 + row) * 128;
+      auto emit_chunk = [&](const uint32_t (&c32)[32], int h) {
+        uint8_t* arow = prow + (h >> 1) * (NQT * 16384);
+        const int q0c = (h & 1) * 4;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = ex2_approx(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new));
+          pk[e >> 1] = pack_half2(x0, x1);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(arow + (((q0c + q) ^ r7) << 4)) = u;
+        }
+      };
+#pragma unroll
+      for (int h = 0; h < NCH; ++h) emit_chunk(sv[h], h);
+      m_used = m_new;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full(t, j & 1));
+    }
+    if (ok && nkv > 0) ok = bar_and(bar_id, 128, __all_sync(0xffffffffu, wait_pv(nkv - 1)));
+    if (ok) {
+      // O^T columns of this tile -> shared memory as [row][d] (P buffers are free now), then each
+      // thread normalises its row by the ones-row sum (d row p.d) and stores it
+      tc_fence_after();
+      float* ob = reinterpret_cast<float*>(sP) + t * (128 * 65);
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_ot + c, r);
+        tmem_wait_ld();
+        if (lane < 16) {
+          const int d = lg * 16 + lane;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ob[(c + e) * 65 + d] = __uint_as_float(r[e]);
+        }
+      }
+      bar_sync_n(bar_id, 128);
+      const int qi = q0 + t * 128 + row;
+      if (qi < p.Sq) {
+        const float inv = 1.f / ob[row * 65 + p.d];
+        const int b = bh / p.heads, h = bh % p.heads;
+        __half* dst = p.o + ((size_t)b * p.Sq + qi) * p.ld_o + (size_t)h * p.d;
+        for (int c = 0; c < p.d; c += 8) {
+          const float* src = ob + row * 65 + c;
+          uint4 u;
+          u.x = pack_half2(src[0] * inv, src[1] * inv);
+          u.y = pack_half2(src[2] * inv, src[3] * inv);
+          u.z = pack_half2(src[4] * inv, src[5] * inv);
+          u.w = pack_half2(src[6] * inv, src[7] * inv);
+          *reinterpret_cast<uint4*>(dst + c) = u;
+        }
+      }
     }
   } else {
     // ---------------------------------------------------------------- softmax
@@ -429,7 +619,7 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
   switch (a.d16) {
     case 48:
       if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
-      if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true>>(a, err, s);  // fewer, wider QK^T MMAs
+      if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true, true>>(a, err, s);  // wide QK^T, transposed PV
       return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);  // short key sets (cross-attention)
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
     case 80: return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles
