@@ -75,10 +75,17 @@ struct Cfg {
   static constexpr int kBRows = PAIR ? BN / 2 : BN;  // W rows held by this CTA
   static constexpr uint32_t kBTileBytes = kBRows * BK * 2;
   static constexpr uint32_t kB8Bytes = W8 ? BN * BK : 0;  // int8 staging tile
-  static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes + kB8Bytes;
-  // bytes TMA delivers per stage (PAIR: counted on the even CTA's barrier for both CTAs)
+  static constexpr uint32_t kSubBytes = kATileBytes + kBTileBytes + kB8Bytes;  // one 64-deep k-block
+  // bytes TMA delivers per k-block (PAIR: counted on the even CTA's barrier for both CTAs)
   static constexpr uint32_t kTxBytes =
       PAIR ? 2 * (kATileBytes + kBTileBytes) : kATileBytes + (W8 ? kB8Bytes : kBTileBytes);
+  // k-blocks per pipeline stage. Every mbarrier wait in the MMA-issuing thread leaves the tensor
+  // pipe a bubble (measured on B200: a 64-deep stage costs >= ~500 cycles with a wait per stage,
+  // ~340 per k-block with one wait per two k-blocks, against 256/320 cycles of MMA work at
+  // N = 128/160), so a stage holds two k-blocks (8 MMAs per wait) wherever three such stages
+  // fit in shared memory.
+  static constexpr int kG = (!W8 && (232448 - 1024 - 512) / (2 * kSubBytes) >= 3) ? 2 : 1;
+  static constexpr uint32_t kStageBytes = kG * kSubBytes;
   // as many stages as shared memory holds: TMA latency from L2 needs deep pipelines
   static constexpr int kStages = (232448 - 1024 - 512) / kStageBytes > 12 ? 12 : (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kAccStride = BN <= 16 ? 16 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
@@ -202,9 +209,11 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int G = C::kG;  // k-blocks per stage; k-block g of stage s lives in slot s * G + g
+  static_assert(!W8 || G == 1, "wo8 converters walk one k-block per stage");
   uint8_t* sA = smem;
-  uint8_t* sB = smem + S * kATileBytes;
-  uint8_t* sB8 = sB + S * C::kBTileBytes;  // int8 staging (wo8 only)
+  uint8_t* sB = smem + S * G * kATileBytes;
+  uint8_t* sB8 = sB + S * G * C::kBTileBytes;  // int8 staging (wo8 only)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB8 + S * C::kB8Bytes);
   // bars: full[S], empty[S], tfull[2], tempty[2], drain, conv[S] (wo8: fp16 B tile ready)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
@@ -293,37 +302,44 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           img0 = m0 / hw;
           y0 = (m0 % hw) / p.W;
         }
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += G, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
+          const int nsub = min(G, kb1 - kb);  // k-blocks in this stage (the unit's last may be short)
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(s), C::kTxBytes);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(s), (uint32_t)nsub * C::kTxBytes);
           issued[s] = true;
           last_phase[s] = ph;
           const uint32_t fb = PAIR ? mapa_shared(full_bar(s), 0) : full_bar(s);
-          const uint32_t dA = smem_u32(sA + s * kATileBytes);
-          const uint32_t dB = W8 ? smem_u32(sB8 + s * C::kB8Bytes) : smem_u32(sB + s * C::kBTileBytes);
-          const int tap = kb / kb_per_tap;
-          const int cc = (kb % kb_per_tap) * BK;
-          const bool second = cc >= p.cin0;
-          const CUtensorMap* ma = second ? &map_a1 : &map_a0;
-          const int ch = second ? cc - p.cin0 : cc;
-          if constexpr (PAIR) {
-            if (p.taps == 9) {
-              const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-              tma_load_4d_pair(dA, ma, fb, ch, dx, y0 + dy, img0);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            if (g >= nsub) break;
+            const int k = kb + g;
+            const int slot = s * G + g;
+            const uint32_t dA = smem_u32(sA + slot * kATileBytes);
+            const uint32_t dB = W8 ? smem_u32(sB8 + slot * C::kB8Bytes) : smem_u32(sB + slot * C::kBTileBytes);
+            const int tap = k / kb_per_tap;
+            const int cc = (k % kb_per_tap) * BK;
+            const bool second = cc >= p.cin0;
+            const CUtensorMap* ma = second ? &map_a1 : &map_a0;
+            const int ch = second ? cc - p.cin0 : cc;
+            if constexpr (PAIR) {
+              if (p.taps == 9) {
+                const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+                tma_load_4d_pair(dA, ma, fb, ch, dx, y0 + dy, img0);
+              } else {
+                tma_load_2d_pair(dA, ma, fb, ch, m0);
+              }
+              tma_load_2d_pair(dB, &map_w, fb, k * BK, n0);
             } else {
-              tma_load_2d_pair(dA, ma, fb, ch, m0);
+              if (p.taps == 9) {
+                const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+                tma_load_4d(dA, ma, fb, ch, dx, y0 + dy, img0);
+              } else {
+                tma_load_2d(dA, ma, fb, ch, m0);
+              }
+              tma_load_2d(dB, &map_w, fb, k * BK, n0);
             }
-            tma_load_2d_pair(dB, &map_w, fb, kb * BK, n0);
-          } else {
-            if (p.taps == 9) {
-              const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-              tma_load_4d(dA, ma, fb, ch, dx, y0 + dy, img0);
-            } else {
-              tma_load_2d(dA, ma, fb, ch, m0);
-            }
-            tma_load_2d(dB, &map_w, fb, kb * BK, n0);
           }
         }
       }
@@ -353,20 +369,28 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         if (!got) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; kb += G, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
+          const int nsub = min(G, kb1 - kb);
           if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
           if (W8 && !mbar_wait(conv_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t da = sdesc_sw128(smem_u32(sA + s * kATileBytes), 16, 1024);
-          const uint64_t db = sdesc_sw128(smem_u32(sB + s * C::kBTileBytes), 16, 1024);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            if constexpr (PAIR)
-              mma_f16_ss2(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-            else
-              mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          for (int g = 0; g < G; ++g) {
+            if (g >= nsub) break;
+            const int slot = s * G + g;
+            const uint64_t da = sdesc_sw128(smem_u32(sA + slot * kATileBytes), 16, 1024);
+            const uint64_t db = sdesc_sw128(smem_u32(sB + slot * C::kBTileBytes), 16, 1024);
+            const uint32_t first = (kb == kb0 && g == 0) ? 1u : 0u;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint32_t accum = (first && k == 0) ? 0u : 1u;
+              if constexpr (PAIR)
+                mma_f16_ss2(d_tmem, da + 2ull * k, db + 2ull * k, idesc, accum);
+              else
+                mma_f16_ss(d_tmem, da + 2ull * k, db + 2ull * k, idesc, accum);
+            }
           }
           if constexpr (PAIR)
             mma_commit2_mc(empty_bar(s), 0x3);  // frees stage s in both CTAs
@@ -602,9 +626,9 @@ struct TileChoice {
 
 // Cost model, fitted to launch times measured on B200 over the SD1.5 UNet's GEMM and conv shapes
 // (graph replay, 1-CTA and CTA-pair tiles of width 64..256, 1..32 K splits; median error 5 %):
-//   t = waves * (k-blocks per unit * t_kb + t_unit) + (splits > 1 ? 5.8 us + 0.213 us per MB of partials : 0)
-// A 64-deep k-block costs ~0.33-0.39 us per CTA at every tile width (the tensor pipe does not get
-// cheaper per instruction for narrow tiles), so wider tiles win until they leave SMs idle; t_unit
+//   t = waves * (k-blocks per unit * t_kb + t_unit) + (splits > 1 ? 5.5 us + 0.181 us per MB of partials : 0)
+// Tiles whose stages hold two k-blocks (1-CTA widths <= 160, every CTA-pair width) cost ~0.26-0.29 us
+// per 64-deep k-block and CTA; the 1-CTA 192/256 tiles, one k-block per stage, 0.33-0.38. t_unit
 // (pipeline fill + epilogue) grows with the tile width.
 struct TileCost {
   int bn;
@@ -612,9 +636,9 @@ struct TileCost {
   double us_per_kb, us_per_unit;
 };
 constexpr TileCost kTileCosts[] = {
-    {256, false, 0.323, 6.09}, {192, false, 0.393, 3.89}, {160, false, 0.353, 3.52}, {128, false, 0.355, 2.90},
-    {64, false, 0.341, 1.27},  {256, true, 0.323, 7.15},  {192, true, 0.382, 4.36},  {160, true, 0.353, 3.75},
-    {128, true, 0.347, 3.20},
+    {256, false, 0.334, 6.52}, {192, false, 0.383, 4.23}, {160, false, 0.269, 3.99}, {128, false, 0.265, 2.79},
+    {64, false, 0.267, 1.35},  {256, true, 0.293, 6.92},  {192, true, 0.276, 5.20},  {160, true, 0.269, 4.42},
+    {128, true, 0.260, 3.32},
 };
 
 TileChoice choose_tiles(const GemmArgs& a) {
@@ -647,7 +671,7 @@ TileChoice choose_tiles(const GemmArgs& a) {
       if (real_sp != sp) continue;
       const int waves = (tiles * sp + teams - 1) / teams;
       double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit);
-      if (sp > 1) t += 5.8 + 0.213 * ((double)sp * a.M * a.N * 4.0 / 1e6);
+      if (sp > 1) t += 5.5 + 0.181 * ((double)sp * a.M * a.N * 4.0 / 1e6);
       if (t < best_t) {
         best_t = t;
         best.bn = bn;
