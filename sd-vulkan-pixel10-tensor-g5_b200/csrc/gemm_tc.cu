@@ -23,6 +23,8 @@
 #include <cmath>
 #include <cstdio>
 
+#include <cooperative_groups.h>
+
 #include "sdg_kernels.h"
 #include "sdg_launch.h"
 #include "sdg_ptx.cuh"
@@ -34,6 +36,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+constexpr int kMaxCsplitCtas = 8;  // cluster K split: at most the portable cluster size
 constexpr uint32_t kATileBytes = BM * BK * 2;  // 16 KB
 
 struct GemmDev {
@@ -56,6 +59,7 @@ struct GemmDev {
   int head_C, heads, head_d, head_dp;
   int head_vt, head_d16, head_spad;
   int splits, kb_per_split;  // split-K
+  int csplit;                // > 1: K split over the CTAs of a cluster, reduced through DSMEM
   float* ws;                 // [splits][M][N] fp32 partials when splits > 1
   const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
@@ -204,9 +208,17 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
   using C = Cfg<BN, W8, PAIR>;
   constexpr int TM = PAIR ? 2 * BM : BM;  // output rows per unit
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  const int team = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // pair (or CTA) index
-  const int nteams = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // cluster K split (1-CTA tiles only): the csp CTAs of a cluster share one output tile, CTA krank
+  // computes the k-blocks [krank * kb_per_split, ...) and the partial tiles are summed through
+  // distributed shared memory; one tile per cluster (no persistent loop)
+  const int csp = PAIR ? 1 : p.csplit;
+  const int krank = csp > 1 ? (int)cluster_ctarank() : 0;
+  const int team = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x / csp;  // pair / cluster / CTA index
+  const int nteams = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x / csp;
   constexpr int S = C::kStages;
+  constexpr int kRedStride = BN + 4;  // floats per partial row in the cluster K-split reduction
+  static_assert((size_t)(BM + kMaxCsplitCtas - 1) * kRedStride * 4 <= (size_t)S * C::kStageBytes,
+                "cluster K-split slots exceed stage memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int G = C::kG;  // k-blocks per stage; k-block g of stage s lives in slot s * G + g
@@ -231,13 +243,13 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
   const int num_m = (p.M + TM - 1) / TM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_mn = num_m * num_n;
-  const int num_units = num_mn * p.splits;
+  const int num_units = csp > 1 ? num_mn : num_mn * p.splits;
   const int kb_per_tap = (p.cin0 + p.cin1) / BK;
   const int KB = p.K / BK;
   // unit -> (m block, n block, k range); m fastest so co-resident CTAs share W tiles
   auto decode = [&](int unit, int& m_blk, int& n_blk, int& kb0, int& kb1) {
-    const int ks = unit / num_mn;
-    const int r = unit - ks * num_mn;
+    const int ks = csp > 1 ? krank : unit / num_mn;
+    const int r = csp > 1 ? unit : unit - ks * num_mn;
     m_blk = r % num_m;
     n_blk = r / num_m;
     kb0 = ks * p.kb_per_split;
@@ -458,13 +470,16 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       const int img = m / p.rows_per_image;
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
-      if (p.splits == 1 && p.epi != kEpiGeglu) epi_prefetch<C::kChunk>(p, m, img, n0 + eh * C::kChunk, mvalid);
+      if (p.splits == 1 && csp == 1 && p.epi != kEpiGeglu) epi_prefetch<C::kChunk>(p, m, img, n0 + eh * C::kChunk, mvalid);
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
       constexpr int CH = C::kChunk;
-      if (p.epi == kEpiGeglu) {
+      if (csp > 1) {
+        // cluster K split: the partial tile stays in TMEM until every CTA of the cluster is
+        // past its main loop (reduction below)
+      } else if (p.epi == kEpiGeglu) {
         constexpr int HALF = BN / 2;
         const int nout0 = n_blk * HALF;
 #pragma unroll 1
@@ -553,6 +568,67 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     }
   }
 
+  if (csp > 1) {
+    // Cluster K split. CTA q of the cluster owns rows [q * rpc, (q + 1) * rpc) of the tile
+    // (rpc = ceil(128 / csp)); every CTA pushes each partial row to its owner's stage memory,
+    // slot [krank], and the owner sums the slots in rank order (deterministic) and applies
+    // the fused epilogue. Stage memory is reused, so the pushes start only once every CTA of
+    // the cluster is past its main loop.
+    const int rpc = (BM + csp - 1) / csp;
+    const bool epi_warp = warp >= 2 && warp < 2 + C::kEpiWarps && team < num_units;
+    tc_fence_before();
+    cluster_sync_all();
+    if (epi_warp) {
+      tc_fence_after();
+      const int lg = warp & 3;
+      const int row = lg * 32 + lane;
+      constexpr int kSplit = C::kEpiWarps / 4;
+      const int eh = (warp - 2) >> 2;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(lg * 32) << 16);
+      const int owner = row / rpc;
+      const uint32_t dst_row = mapa_shared(
+          smem_u32(smem) + (uint32_t)(((krank * rpc) + (row - owner * rpc)) * kRedStride) * 4u, (uint32_t)owner);
+      constexpr int CH = C::kChunk;
+#pragma unroll 1
+      for (int c = eh * CH; c < BN; c += kSplit * CH) {
+        uint32_t r[32];
+        if constexpr (CH == 32) {
+          tmem_ld32(t_row + c, r);
+        } else {
+          uint32_t t16[16];
+          tmem_ld16(t_row + c, t16);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = t16[j];
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < CH / 4; ++q)
+          st_cluster_v4(dst_row + (uint32_t)(c + 4 * q) * 4u, r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      }
+    }
+    cluster_sync_all();  // every partial row is in its owner's shared memory
+    if (epi_warp) {
+      int m_blk, n_blk, kb0, kb1;
+      decode(team, m_blk, n_blk, kb0, kb1);
+      const int r0 = krank * rpc, nrows = min(rpc, BM - r0);
+      const int ngrp = BN / 8;
+      const float* buf = reinterpret_cast<const float*>(smem);
+      for (int i = threadIdx.x - 64; i < nrows * ngrp; i += C::kEpiWarps * 32) {
+        const int rl = i / ngrp;
+        const int c = (i % ngrp) * 8;
+        const int m = m_blk * BM + r0 + rl;
+        const int n = n_blk * BN + c;
+        if (m >= p.M || n >= p.N) continue;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < csp; ++q) {
+          const float4* src = reinterpret_cast<const float4*>(buf + (size_t)(q * rpc + rl) * kRedStride + c);
+          const float4 a = src[0], b = src[1];
+          v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+        }
+        epilogue8(p, m, m / p.rows_per_image, n, v);
+      }
+    }
+  }
   tc_fence_before();
   __syncwarp();
   if constexpr (PAIR)
@@ -609,7 +685,11 @@ cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMa
     attr_set[dev] = true;
   }
   constexpr int TM = PAIR ? 2 * BM : BM;
-  const int units = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN) * d.splits;
+  const int tiles = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN);
+  if (!PAIR && d.csplit > 1)  // one cluster of csplit CTAs per output tile
+    return launch_kernel(gemm_tc_kernel<BN, W8, PAIR>, dim3(tiles * d.csplit), dim3(C::kThreads), C::kSmem, s,
+                         d.csplit, ma0, ma1, mw, d);
+  const int units = tiles * d.splits;
   const int teams = std::max(1, std::min(units, PAIR ? num_sms() / 2 : num_sms()));
   cudaError_t e = launch_kernel(gemm_tc_kernel<BN, W8, PAIR>, dim3(PAIR ? 2 * teams : teams), dim3(C::kThreads),
                                 C::kSmem, s, PAIR ? 2 : 0, ma0, ma1, mw, d);
@@ -622,6 +702,7 @@ cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMa
 struct TileChoice {
   int bn = 64, splits = 1, kb_per_split = 1;
   bool pair = false;  // 256-row tiles on a CTA pair (cta_group::2)
+  int csplit = 1;     // > 1: K split over a cluster of csplit CTAs per tile, reduced through DSMEM
 };
 
 // Cost model, fitted to launch times measured on B200 over the SD1.5 UNet's GEMM and conv shapes
@@ -641,7 +722,43 @@ constexpr TileCost kTileCosts[] = {
     {128, true, 0.260, 3.32},
 };
 
-TileChoice choose_tiles(const GemmArgs& a) {
+// K split inside a cluster: partial tiles summed through distributed shared memory (no workspace,
+// no second launch). Its cost over the shortened main loop, fitted on B200 like the tile costs
+// (median error 1 us): 0.92 us + 0.62 us per CTA of the cluster + 0.61 us per 128 tile columns.
+constexpr double kCsplitUs = 0.92, kCsplitUsPerCta = 0.62, kCsplitUsPer128Cols = 0.61;
+
+// Clusters of `cs` GEMM CTAs (one CTA per SM) that can be resident at once: a cluster must fit in
+// one GPC, so this is below num_sms() / cs for the larger sizes.
+int cluster_capacity(int cs) {
+  static int cap[64][kMaxCsplitCtas + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || cs < 2 || cs > kMaxCsplitCtas) return std::max(1, num_sms() / std::max(1, cs));
+  if (!cap[dev][cs]) {
+    using C = Cfg<160, false, false>;
+    auto k = gemm_tc_kernel<160, false, false>;
+    int n = 0;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cs * 64);
+      cfg.blockDim = dim3(C::kThreads);
+      cfg.dynamicSmemBytes = C::kSmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = cs;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cap[dev][cs] = n > 0 ? n : std::max(1, num_sms() / cs);
+  }
+  return cap[dev][cs];
+}
+
+TileChoice choose_tiles(const GemmArgs& a, bool allow_ws = true) {
   TileChoice best;
   const int KB = a.K / BK;
   const int sms = num_sms();
@@ -669,15 +786,24 @@ TileChoice choose_tiles(const GemmArgs& a) {
       const int kbs = (KB + sp - 1) / sp;
       const int real_sp = (KB + kbs - 1) / kbs;
       if (real_sp != sp) continue;
-      const int waves = (tiles * sp + teams - 1) / teams;
-      double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit);
-      if (sp > 1) t += 5.5 + 0.181 * ((double)sp * a.M * a.N * 4.0 / 1e6);
-      if (t < best_t) {
-        best_t = t;
-        best.bn = bn;
-        best.splits = sp;
-        best.kb_per_split = kbs;
-        best.pair = tcst.pair;
+      if (sp > 1 && allow_ws) {  // workspace split-K + reduce launch
+        const int waves = (tiles * sp + teams - 1) / teams;
+        const double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit) + 5.5 +
+                         0.181 * ((double)sp * a.M * a.N * 4.0 / 1e6);
+        if (t < best_t) {
+          best_t = t;
+          best = TileChoice{bn, sp, kbs, tcst.pair, 1};
+        }
+      }
+      if (sp == 1 || (!tcst.pair && sp <= kMaxCsplitCtas)) {  // single pass, or cluster split-K
+        const int cap = sp > 1 ? cluster_capacity(sp) : teams;  // resident clusters (sp > 1) or CTAs
+        const int waves = (tiles + cap - 1) / cap;
+        double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit);
+        if (sp > 1) t += kCsplitUs + kCsplitUsPerCta * sp + kCsplitUsPer128Cols * bn / 128.0;
+        if (t < best_t) {
+          best_t = t;
+          best = TileChoice{bn, 1, sp > 1 ? kbs : KB, tcst.pair, sp};
+        }
       }
     }
   }
@@ -708,10 +834,8 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   if (a.epi != kEpiNchwF32 && a.epi != kEpiGeglu && a.N % 16 != 0) return cudaErrorInvalidValue;
   if ((a.epi == kEpiPlain || a.epi == kEpiHeads) && a.N > 16 && a.N % 32 != 0) return cudaErrorInvalidValue;
   TileChoice tc = choose_tiles(a);
-  if (tc.splits > 1 && (a.ws == nullptr || a.ws_bytes < (size_t)tc.splits * a.M * a.N * sizeof(float))) {
-    tc.splits = 1;  // no workspace: single pass
-    tc.kb_per_split = a.K / BK;
-  }
+  if (tc.splits > 1 && (a.ws == nullptr || a.ws_bytes < (size_t)tc.splits * a.M * a.N * sizeof(float)))
+    tc = choose_tiles(a, false);  // no workspace: single pass or cluster split
   const int bn = tc.bn;
   if (a.epi == kEpiGeglu && (a.N % bn != 0)) return cudaErrorInvalidValue;
   if (a.epi == kEpiHeads && (a.head_d % 8 != 0 || a.head_C % 8 != 0 || a.head_dp < a.head_d ||
@@ -732,6 +856,7 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.head_C = a.head_C; d.heads = a.heads; d.head_d = a.head_d; d.head_dp = a.head_dp;
   d.head_vt = a.head_vt; d.head_d16 = a.head_d16; d.head_spad = a.head_spad;
   d.splits = tc.splits; d.kb_per_split = tc.kb_per_split; d.ws = a.ws;
+  d.csplit = tc.csplit;
   d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
   if (a.w8 && !a.wscale) return cudaErrorInvalidValue;
