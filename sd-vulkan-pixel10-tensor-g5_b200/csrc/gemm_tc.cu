@@ -188,6 +188,90 @@ __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int img, int 
   *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + n) = pack8(v);
 }
 
+// Epilogue operands of one CH-column chunk of row m, fetched before the accumulator is read so
+// the global-load latencies overlap each other and the TMEM load (loading them per 8-column
+// group, after each group's store, serialises one L2 round trip per group).
+template <int CH>
+struct EpiIn {
+  float4 b[CH / 4];   // bias + per-image row bias
+  uint4 res[CH / 8];  // residual (fp16)
+};
+
+template <int CH>
+__device__ __forceinline__ void epi_load(const GemmDev& p, int m, int img, int n, bool mvalid, EpiIn<CH>& in) {
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < CH / 4; ++q) {
+    const bool ok = n + 4 * q < p.N;
+    in.b[q] = (ok && p.bias) ? __ldg(reinterpret_cast<const float4*>(p.bias + n) + q) : z;
+  }
+  if (p.rowbias) {  // resnet conv1: the time-embedding projection per image
+#pragma unroll
+    for (int q = 0; q < CH / 4; ++q) {
+      if (n + 4 * q >= p.N) break;
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p.rowbias + (size_t)img * p.rowbias_ld + n) + q);
+      in.b[q].x += t.x; in.b[q].y += t.y; in.b[q].z += t.z; in.b[q].w += t.w;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < CH / 8; ++g)
+    in.res[g] = (mvalid && p.residual && n + 8 * g < p.N)
+                    ? __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.ld_res + n) + g)
+                    : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Fused epilogue of one chunk (plain or attention-head outputs) from the accumulator words r and
+// the prefetched operands; same arithmetic as epilogue8.
+template <int CH>
+__device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int n, const uint32_t* r, const EpiIn<CH>& in) {
+#pragma unroll
+  for (int g = 0; g < CH / 8; ++g) {
+    const int ng = n + g * 8;
+    if (ng >= p.N) break;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+    if (p.wscale) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + min(ng + j, p.N - 1));
+    }
+    const float4 b0 = in.b[2 * g], b1 = in.b[2 * g + 1];
+    v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+    v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+    if (p.residual) {
+      const __half2* h = reinterpret_cast<const __half2*>(&in.res[g]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        v[2 * e] += f.x;
+        v[2 * e + 1] += f.y;
+      }
+    }
+    if (p.act == 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+    }
+    if (p.epi == kEpiHeads) {
+      const int s_idx = m - img * p.rows_per_image;
+      const int which = ng / p.head_C;
+      const int cc = ng - which * p.head_C;
+      const int h = cc / p.head_d;
+      const int jj = cc - h * p.head_d;
+      __half* base = which == 0 ? p.head_out0 : (which == 1 ? p.head_out1 : p.head_out2);
+      if (which == p.head_vt) {
+        __half* dst = base + (((size_t)img * p.heads + h) * p.head_d16 + jj) * p.head_spad + s_idx;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dst[(size_t)e * p.head_spad] = __float2half_rn(v[e]);
+        continue;
+      }
+      __half* dst = base + (((size_t)img * p.heads + h) * p.rows_per_image + s_idx) * p.head_dp + jj;
+      *reinterpret_cast<uint4*>(dst) = pack8(v);
+      continue;
+    }
+    *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + ng) = pack8(v);
+  }
+}
+
 // int8 x4 (one 32-bit word) -> two fp16x2, exact: bias the bytes to unsigned,
 // splice each under the fp16 exponent of 1024 (0x64), subtract 1024 + 128.
 __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& hi) {
@@ -499,11 +583,27 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) { ra[j] = t16a[j]; rg[j] = t16g[j]; }
           }
+          // value / gate biases, one 8-column group ahead of its use (the first group's fetched
+          // while the TMEM load is in flight)
+          auto ldb = [&](int col, float4 (&b)[4]) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4* bv = reinterpret_cast<const float4*>(p.bias + n0 + col);
+            const float4* bg = reinterpret_cast<const float4*>(p.bias + n0 + HALF + col);
+            b[0] = p.bias ? __ldg(bv) : z;
+            b[1] = p.bias ? __ldg(bv + 1) : z;
+            b[2] = p.bias ? __ldg(bg) : z;
+            b[3] = p.bias ? __ldg(bg + 1) : z;
+          };
+          float4 bcur[4], bnext[4];
+          ldb(c, bcur);
           tmem_wait_ld();
           const int nc = nout0 + c;
           if (mvalid && nc < p.N / 2) {
 #pragma unroll
             for (int g = 0; g < CH / 8; ++g) {
+              if (g + 1 < CH / 8) ldb(c + (g + 1) * 8, bnext);
+              const float bav[8] = {bcur[0].x, bcur[0].y, bcur[0].z, bcur[0].w, bcur[1].x, bcur[1].y, bcur[1].z, bcur[1].w};
+              const float bgv[8] = {bcur[2].x, bcur[2].y, bcur[2].z, bcur[2].w, bcur[3].x, bcur[3].y, bcur[3].z, bcur[3].w};
               float v[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -513,11 +613,12 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
                   a *= __ldg(p.wscale + n0 + cj);
                   gt *= __ldg(p.wscale + n0 + HALF + cj);
                 }
-                a += p.bias ? __ldg(p.bias + n0 + cj) : 0.f;
-                gt += p.bias ? __ldg(p.bias + n0 + HALF + cj) : 0.f;
-                v[j] = a * gelu_erf(gt);
+                a += bav[j];
+                gt += bgv[j];                v[j] = a * gelu_erf(gt);
               }
               *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc + g * 8) = pack8(v);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) bcur[q] = bnext[q];
             }
           }
         }
@@ -534,9 +635,16 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) r[j] = t16[j];
           }
-          tmem_wait_ld();
           const int n = n0 + c;
+          const bool fused = p.splits == 1 && p.epi != kEpiNchwF32;
+          EpiIn<CH> in;
+          if (fused) epi_load<CH>(p, m, img, n, mvalid, in);  // in flight with the TMEM load
+          tmem_wait_ld();
           if (!mvalid || n >= p.N) continue;
+          if (fused) {
+            epi_apply<CH>(p, m, img, n, r, in);
+            continue;
+          }
           if (p.splits > 1) {
             // raw fp32 partials; the reduce kernel applies the epilogue
             const int ks = kb0 / p.kb_per_split;
