@@ -88,6 +88,25 @@ struct AttnDev {
   int* err;
 };
 
+
+// Maximum of a score row held as NCH x 32 words: eight independent partial maxima, then a
+// tree, so the dependency chain is 4 * NCH + 3 deep instead of 32 * NCH.
+template <int NCH>
+__device__ __forceinline__ float row_max(const uint32_t (&sv)[NCH][32]) {
+  float pm[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) pm[k] = -INFINITY;
+#pragma unroll
+  for (int h = 0; h < NCH; ++h)
+#pragma unroll
+    for (int e = 0; e < 32; ++e) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(sv[h][e]));
+#pragma unroll
+  for (int k = 4; k; k >>= 1)
+#pragma unroll
+    for (int i = 0; i < k; ++i) pm[i] = fmaxf(pm[i], pm[i + k]);
+  return pm[0];
+}
+
 template <class CF>
 __global__ void __launch_bounds__(CF::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -346,19 +365,14 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
             for (int e = 0; e < 32; ++e)
               if (kbase + 32 * h + e >= p.Sk) sv[h][e] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < NCH; ++h)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sv[h][e]));
-        const float m_cand = mx * p.sl2;
+        const float m_cand = row_max<NCH>(sv) * p.sl2;
         need = m_cand > m_used + kRescale;
         m_new = need ? m_cand : m_used;
         corr = need ? ex2_approx(m_used - m_new) : 1.f;
         corr_s[row] = corr;
       }
-      if (!bar_and(bar_id, 128, mine)) { ok = false; break; }
-      const bool rescale = bar_or(bar_id, 128, need) && j > 0;
+      // a failed wait takes the rescale branch too; the barrier below then ends the loop
+      const bool rescale = bar_or(bar_id, 128, need || !mine) && j > 0;
       // P buffer j%2 was read by PV(j-2); a rescale needs PV(j-1) retired as well
       bool waited = true;
       if (rescale || j >= 2) waited = wait_pv(rescale ? j - 1 : j - 2);
@@ -376,7 +390,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
         tmem_wait_st();
       }
-      if (!bar_and(bar_id, 128, waited)) { ok = false; break; }  // also: every read of corr_s is done
+      if (!bar_and(bar_id, 128, waited && mine)) { ok = false; break; }  // also: every read of corr_s is done
       uint8_t* prow = sP + (j & 1) * NQT * CF::kPTile + (t * 128 + row) * 128;
       auto emit_chunk = [&](const uint32_t (&c32)[32], int h) {
         uint8_t* arow = prow + (h >> 1) * (NQT * 16384);
@@ -478,12 +492,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
           for (int e = 0; e < 32; ++e)
             if (kbase + 32 * h + e >= p.Sk) sv[h][e] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int h = 0; h < NCH; ++h)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sv[h][e]));
-      const float m_cand = mx * p.sl2;
+      const float m_cand = row_max<NCH>(sv) * p.sl2;
       const bool need = m_cand > m_used + kRescale;
       const float m_new = need ? m_cand : m_used;
       const float corr = need ? ex2_approx(m_used - m_new) : 1.f;
