@@ -3,22 +3,26 @@
 // Replaces the reference's conv/matmul family (vk_engine.cpp:578-613;
 // matmul_f32.comp, im2col_f32.comp, winograd_*.comp, addbias*_f32.comp,
 // add_f32.comp, geglu_f32.comp) with one persistent, warp-specialised kernel:
-//   warp 0      TMA producer: A tile 128x64 + W tile BNx64 per stage (SW128)
+//   warp 0      TMA producer: A tile 128x64 + W tile BNx64 per k-block (SW128);
+//               a pipeline stage holds one or two k-blocks
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128,K=16)
-//   warps 2..5  epilogue: tcgen05.ld rows from TMEM, fused bias / per-image
-//               bias / residual / SiLU / GEGLU / head scatter, fp16 stores
+//   warps 2..9  epilogue (two warps per TMEM lane quadrant): tcgen05.ld rows
+//               from TMEM, fused bias / per-image bias / residual / SiLU /
+//               GEGLU / head scatter, fp16 stores
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps
-// the main loop of tile i+1. No cluster multicast is used anywhere.
+// the main loop of tile i+1. No cluster multicast is used anywhere. A CTA pair
+// (cluster of 2, tcgen05.mma.cta_group::2) computes 256-row tiles.
 //
 // Weight-only int8 (wo8): W arrives as int8 by TMA into a staging tile;
-// 4 converter warps (warps 6..9) rewrite it as fp16 (exact) in the swizzled
-// B layout while the MMA runs, and the per-output-channel scale is applied in
-// the epilogue (sum_k a*(q*s) = s * sum_k a*q).
+// 4 converter warps (warps 6..9, leaving warps 2..5 to the epilogue) rewrite
+// it as fp16 (exact) in the swizzled B layout while the MMA runs, and the
+// per-output-channel scale is applied in the epilogue (sum_k a*(q*s) = s * sum_k a*q).
 //
-// Split-K: when M is small (deep UNet levels) the K range is divided among
-// CTAs; each writes fp32 partials to a workspace and a reduce kernel sums the
-// splits in a fixed order and applies the same fused epilogue, so results are
-// deterministic.
+// Split-K (deep UNet levels, small M): the K range is divided either among the
+// 2..8 CTAs of a cluster working on one tile, whose fp32 partial rows are summed
+// through distributed shared memory, or among independent CTAs writing fp32
+// partials to a workspace that a reduce kernel sums. Both sum in a fixed order
+// and apply the same fused epilogue, so results are deterministic.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
