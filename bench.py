@@ -61,20 +61,32 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.lines = []
+        self.lines = []  # (arrival time, csv line)
         self.t = None
+        self.t0 = self.t1 = 0.0
+
+    def _read(self):
+        for ln in iter(self.proc.stdout.readline, ""):
+            self.lines.append((time.time(), ln))
 
     def start(self):
+        """Start sampling every 50 ms; returns once the first sample has arrived (at most 3 s), so
+        the samples kept (those arriving between start() and stop()) cover the timed region."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=lambda: self.lines.extend(iter(self.proc.stdout.readline, "")), daemon=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            deadline = time.time() + 3.0
+            while not self.lines and time.time() < deadline:
+                time.sleep(0.01)
         except FileNotFoundError:
             self.proc = None
+        self.t0 = time.time()
 
     def stop(self):
+        self.t1 = time.time()
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -85,7 +97,9 @@ class ClockSampler:
         self.t.join(timeout=2)
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ts, ln in self.lines:
+            if ts < self.t0 or ts > self.t1 + 0.06:
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue

@@ -149,6 +149,12 @@ SDG_API int sdg_profile(sdg_engine* e, int B, int H, int W, sdg_profile_row* row
 /* Number of kernel launches of one forward at (B,H,W) (after a forward ran). */
 SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
 
+/* No reference counterpart (introspection for tests and tuning): how the GEMM tile
+ * chooser runs an M x N x K product (taps = 9 for a 3x3 convolution, K = 9 * Cin) on
+ * the current device: out4 = {tile width, CTA pair (0/1), workspace K splits, cluster
+ * K splits}; with_workspace = 0 asks for the choice when no split-K workspace is given. */
+SDG_API int sdg_gemm_plan(int M, int N, int K, int taps, int with_workspace, int* out4);
+
 /* --- operator surface (device pointers, fp16 NHWC, stream may be NULL) -------------
  * Replaces the engine's internal op wrappers conv / matmul / groupnorm(_silu) /
  * layernorm / attention op / addbias / addv / concat / upsample

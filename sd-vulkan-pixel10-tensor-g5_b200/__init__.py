@@ -73,6 +73,7 @@ _SIGS = {
     "sdg_lcm_denoise_ex": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "sdg_profile": (_I, [_P, _I, _I, _I, ctypes.POINTER(ProfileRow), _I]),
     "sdg_forward_launches": (_I, [_P, _I, _I, _I]),
+    "sdg_gemm_plan": (_I, [_I, _I, _I, _I, _I, _P]),
     "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, ctypes.c_size_t, _P,
                         _P]),
     "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
@@ -269,6 +270,13 @@ def conv2d(x, w, bias, Co: int, k: int = 3, stride: int = 1, x2=None, rowbias=No
                            _ptr(residual), act, _ptr(out), _ptr(col_scratch), _ptr(workspace), wsb, _ptr(err_word),
                            _stream(stream)))
     return out
+
+
+def gemm_plan(M: int, N: int, K: int, taps: int = 1, workspace: bool = True) -> Dict[str, int]:
+    """The tile chooser's plan for an M x N x K GEMM (taps=9: 3x3 conv, K = 9*Cin) on the current device."""
+    out = (ctypes.c_int * 4)()
+    check(lib().sdg_gemm_plan(M, N, K, taps, 1 if workspace else 0, ctypes.addressof(out)))
+    return {"bn": out[0], "pair": out[1], "splits": out[2], "csplit": out[3]}
 
 
 def linear(x, w, bias=None, residual=None, act: int = 0, out=None, workspace=None, err_word=None, stream=None):

@@ -142,6 +142,16 @@ static int linear_common(const char* name, const uint16_t* x, int M, int K, cons
   return cuda_status(sdg::launch_gemm(a, err, static_cast<cudaStream_t>(stream)), name);
 }
 
+SDG_API int sdg_gemm_plan(int M, int N, int K, int taps, int with_workspace, int* out4) {
+  if (!out4 || M <= 0 || N <= 0 || K <= 0 || K % 64 || !(taps == 1 || taps == 9) || K % (64 * taps))
+    return sdg::op_fail(SDG_ERR_ARG, "gemm_plan: bad arguments");
+  sdg::GemmArgs a;
+  a.M = M; a.N = N; a.K = K; a.taps = taps; a.cin0 = K / taps;
+  const sdg::GemmPlan pl = sdg::gemm_plan(a, with_workspace != 0);
+  out4[0] = pl.bn; out4[1] = pl.pair; out4[2] = pl.splits; out4[3] = pl.csplit;
+  return SDG_OK;
+}
+
 SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
                        const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
                        int* err_word, void* stream) {

@@ -931,6 +931,12 @@ size_t gemm_workspace_bytes(const GemmArgs& a) {
   return t.splits > 1 ? (size_t)t.splits * a.M * a.N * sizeof(float) : 0;
 }
 
+GemmPlan gemm_plan(const GemmArgs& a, bool with_workspace) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK) return GemmPlan{0, 0, 0, 0};
+  const TileChoice t = choose_tiles(a, with_workspace);
+  return GemmPlan{t.bn, t.pair ? 1 : 0, t.splits, t.csplit};
+}
+
 int gemm_launch_count(const GemmArgs& a) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK) return 1;
   const TileChoice t = choose_tiles(a);

@@ -59,6 +59,11 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s);
 size_t gemm_workspace_bytes(const GemmArgs& a);
 // Kernel launches launch_gemm issues for these arguments (1, or 2 with split-K).
 int gemm_launch_count(const GemmArgs& a);
+// The tile chooser's decision: tile width, CTA pair, workspace K splits, cluster K splits.
+struct GemmPlan {
+  int bn, pair, splits, csplit;
+};
+GemmPlan gemm_plan(const GemmArgs& a, bool with_workspace);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
 // tensors. stats: groupnorm_scratch_bytes() bytes; receives (mean, rstd) per

@@ -242,3 +242,35 @@ def test_conv3x3_splitk_rowbias_residual(sdg, cuda, gen, B, C, H):
     torch.cuda.synchronize()
     ref = F.conv2d(x.float(), w.float(), b, padding=1) + rb[:, :, None, None] + res.float()
     assert rel(nchw(y), ref) < TOL
+
+
+# ---------------------------------------------------------------- every K-split path of the tile chooser
+# (M, N, K): UNet GEMM / conv3x3 shapes (a conv's K is 9 * Cin; the chooser sees only M, N, K)
+SPLIT_SHAPES = [(128, 1280, 1280), (128, 1280, 11520), (512, 1280, 5120), (512, 1280, 11520), (2048, 640, 5760),
+                (154, 640, 768), (8192, 320, 320), (128, 1280, 23040)]
+
+
+def _plan_kind(pl):
+    return "cluster" if pl["csplit"] > 1 else ("workspace" if pl["splits"] > 1 else "single")
+
+
+def test_gemm_plan_covers_every_split_path(sdg, cuda):
+    kinds = {_plan_kind(sdg.gemm_plan(M, N, K)) for M, N, K in SPLIT_SHAPES}
+    assert kinds == {"cluster", "workspace", "single"}, kinds
+    for M, N, K in SPLIT_SHAPES:  # without a workspace the chooser never asks for one
+        assert sdg.gemm_plan(M, N, K, workspace=False)["splits"] == 1
+
+
+@pytest.mark.parametrize("with_ws", [True, False])
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+def test_linear_every_split_path(sdg, cuda, gen, M, N, K, with_ws):
+    x = rnd(M, K, g=gen).half()
+    w = rnd(N, K, std=1 / math.sqrt(K), g=gen).half()
+    b = rnd(N, std=0.1, g=gen).float()
+    r = rnd(M, N, g=gen).half()
+    ws = torch.empty(32 * M * N, dtype=torch.float32, device=cuda) if with_ws else None
+    y = sdg.linear(x, w, b, residual=r, workspace=ws)
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().T + b + r.float()
+    err = rel(y, ref)
+    assert err < TOL, (err, sdg.gemm_plan(M, N, K, workspace=with_ws))
