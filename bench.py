@@ -126,23 +126,25 @@ def make_engine(sdg, device, wo8=False):
     return eng, w
 
 
-def cpu_oracle_forward_rate(w, threads, budget_s=30.0):
-    """Time the fp32 oracle forward (config 0) on host cores; returns (fwd/s, sample str)."""
+def cpu_oracle_forward_rate(w, threads, runs=3):
+    """Time the fp32 oracle forward (config 0) on host cores: 1 warm-up forward, then the median
+    of `runs` timed forwards; returns (fwd/s, sample str)."""
     import torch
     from oracle import unet_ref as R
     from oracle import weights as Wt
     torch.set_num_threads(threads)
     lat, t, ctx = Wt.make_inputs(B, H, W, seed=0)
     wf = {k: v.float() for k, v in w.items()}   # fp16-rounded weights held in fp32
-    n, t0 = 0, time.perf_counter()
+    times = []
     with torch.no_grad():
-        while True:
+        R.unet_forward(lat, t, ctx, wf)          # warm-up
+        for _ in range(runs):
+            t0 = time.perf_counter()
             R.unet_forward(lat, t, ctx, wf)
-            n += 1
-            el = time.perf_counter() - t0
-            if el > budget_s * 0.5 or n >= 2:
-                break
-    return n / el, f"{n} full B=2 64x64 fp32 oracle forward(s), {el:.1f} s"
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return 1.0 / med, (f"median of {runs} full B=2 64x64 fp32 oracle forwards after 1 warm-up "
+                       f"({', '.join(f'{x:.2f}' for x in times)} s)")
 
 
 def run_reference_arm(args):
@@ -173,13 +175,84 @@ def run_reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
         "warmup": 1, "ms_per_step": 1000.0 * el / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE config 0)",
-        "config": config_dict(args.gpus),
+        "config": reference_config(),
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference Vulkan engine unavailable on this box (no graphics stack); timed arm = CPU restatement "
                 "of vk_engine.cpp runGraph (oracle/unet_ref.py) in PyTorch fp32 on all host threads",
     }))
     return 0
+
+
+def reference_config():
+    """The work the reference arm actually does: one B=2 forward per step in one CPU process (rank 0;
+    under torchrun the other ranks exit without work)."""
+    return {"workload": "SD1.5 UNet forward, B=2 CFG pair, 64x64 latent, 77x768 context, t=999 (BASELINE config 0)",
+            "global_batch": 2, "latent": [H, W], "context": [77, 768],
+            "parallelism": "one CPU process on rank 0, all host threads (other ranks do no work)"}
+
+
+def config3_inputs(n, H3=64, steps=4):
+    """BASELINE config 3 inputs for n images, identical on every rank: per-image seeded latent
+    ~N(0,1), per-image seeded conditional context, one shared unconditional context (LayerNorm per
+    token), and host-generated per-image noise for the re-noising between LCM steps."""
+    lat = np.empty((n, 4, H3, H3), np.float32)
+    cond = np.empty((n, 77, 768), np.float32)
+    noise = np.empty((steps - 1, n, 4, H3, H3), np.float32)
+    for i in range(n):
+        g = np.random.default_rng(1000 + i)
+        lat[i] = g.standard_normal((4, H3, H3), dtype=np.float32)
+        c = g.standard_normal((77, 768), dtype=np.float32)
+        cond[i] = (c - c.mean(-1, keepdims=True)) / np.sqrt(c.var(-1, keepdims=True) + 1e-5)
+        noise[:, i] = g.standard_normal((steps - 1, 4, H3, H3), dtype=np.float32)
+    u = np.random.default_rng(999).standard_normal((77, 768), dtype=np.float32)
+    u = (u - u.mean(-1, keepdims=True)) / np.sqrt(u.var(-1, keepdims=True) + 1e-5)
+    unc = np.ascontiguousarray(np.broadcast_to(u, (n, 77, 768)))
+    return lat, cond, unc, noise
+
+
+def run_config3(eng, sdg, dev, world, rank, sizes=(8, 16, 64), steps=4, cfg=1.5):
+    """BASELINE config 3 across the ranks: batches of 8/16/64 images, each rank denoises its shard with
+    the 4-step LCM loop through the host API (Engine.lcm_denoise: batch-CFG forwards, CFG combine and
+    LCM update on the device, H2D/D2H of its shard included) and the final latents are all-gathered
+    over NCCL (multigpu.lcm_generate). Host wall clock per rank between barriers, max over ranks; the
+    gather's own time is reported beside. Rank 0 then recomputes every rank's shard alone (same
+    chunking) and checks the gathered latents bit for bit."""
+    import torch
+    import torch.distributed as dist
+    mg = sdg.multigpu
+    out = {"timing": "host wall clock per rank (denoise via the host API + NCCL all_gather), max over ranks",
+           "steps": steps, "cfg": cfg, "forwards_per_image": 2 * steps, "batches": {}}
+    for n in sizes:
+        lat, cond, unc, noise = config3_inputs(n, H, steps)
+        mg.lcm_generate(eng.lcm_denoise, lat, cond, unc, noise, steps=steps, cfg=cfg, device=dev)  # warm-up
+        if world > 1:
+            dist.barrier()
+        tm = {}
+        t0 = time.perf_counter()
+        got = mg.lcm_generate(eng.lcm_denoise, lat, cond, unc, noise, steps=steps, cfg=cfg, device=dev, timings=tm)
+        tot = time.perf_counter() - t0
+        v = torch.tensor([tot, tm["denoise_s"], tm["gather_s"]], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        tot, den, gat = (float(x) for x in v.tolist())
+        rec = {"images": n, "images_per_gpu": mg.shard(n, world, 0)[1], "s": tot, "images_per_s": n / tot,
+               "unet_fwd_per_s": n * steps / tot, "denoise_s_max": den, "gather_s_max": gat,
+               "gather_share": gat / tot}
+        if rank == 0:
+            ref = []
+            for r in range(world):          # each rank's shard, recomputed here with the same chunking
+                s0, c = mg.shard(n, world, r)
+                for a in range(s0, s0 + c, 32):
+                    b = min(s0 + c, a + 32)
+                    ref.append(eng.lcm_denoise(lat[a:b], cond[a:b], unc[a:b], np.ascontiguousarray(noise[:, a:b]),
+                                               steps=steps, cfg=cfg))
+            ref = np.concatenate(ref, 0)
+            rec["gathered_bit_identical_to_1gpu"] = bool(got.shape == ref.shape and np.array_equal(got, ref))
+        out["batches"][str(n)] = rec
+        if world > 1:
+            dist.barrier()
+    return out
 
 
 def config_dict(n, wo8=False):
@@ -199,6 +272,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--wo8", action="store_true", help="weight-only int8 engine (BASELINE config 4)")
+    ap.add_argument("--no-config3", action="store_true", help="skip the config-3 LCM batches (8/16/64 images)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
@@ -278,35 +352,52 @@ def main():
     h2d = n_lat.nbytes + n_ctx.nbytes + n_t.nbytes
     d2h = out_host.nbytes
 
-    # ---- roofline of the dominant kernel: gemm_tc_kernel's 3x3 implicit-GEMM launches (CONV3), timed per
-    # launch with CUDA events in a graph replay of the forward (sdg_profile); algorithmic FLOPs per launch
-    prof = eng.profile(B, H, W)
-    conv_ms, conv_n, conv_fl = prof["CONV3"][0], prof["CONV3"][1], prof["CONV3"][2]
-    gemm_ms = sum(prof[c][0] for c in ("CONV3", "GEMM") if c in prof)
-    gemm_fl = sum(prof[c][2] for c in ("CONV3", "GEMM") if c in prof)
-    gemm_n = sum(prof[c][1] for c in ("CONV3", "GEMM") if c in prof)
+    # ---- roofline of the dominant kernel, gemm_tc_kernel (every conv / linear launch of the forward, with
+    # its split-K reduce launches): the forward's launches of a category are recorded with their arguments
+    # and replayed alone as a CUDA graph, back to back, between two CUDA events on the engine's stream
+    # (sdg_profile_category) -- no per-launch events; algorithmic FLOPs = 2*M*N*K per launch
     hbm, tc_burst, tc_sust, src = peaks()
-    achieved = conv_fl / (conv_ms / 1000.0) / 1e12 if conv_ms > 0 else None
-    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel, conv3x3 implicit-GEMM launches",
-                "achieved": achieved, "peak": tc_burst, "unit": "TFLOP/s",
-                "frac": (achieved / tc_burst) if achieved else None, "peak_source": f"{src} bf16_tflops (burst)",
+    cats = {}
+    for c in ("CONV3+GEMM", "CONV3", "GEMM", "ATTN", "GN", "LN", "GEMV", "MISC"):
+        try:
+            cats[c] = eng.profile_category(c, B, H, W, reps=10)
+        except sdg.SdgError:
+            pass
+    g_ms, g_n, g_fl, _ = cats["CONV3+GEMM"]
+    achieved = g_fl / (g_ms / 1000.0) / 1e12
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel: every conv3x3 / conv1x1 / linear launch of the forward",
+                "achieved": achieved, "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved / tc_burst,
+                "peak_source": f"{src} bf16_tflops (burst)",
+                "timing": "the forward's GEMM launches replayed alone as a CUDA graph (CUDA events around 10 "
+                          "replays), ms per forward " + f"{g_ms:.4f}",
                 "traffic": CONV_TRAFFIC_PER_LAUNCH, "traffic_note": CONV_TRAFFIC_NOTE,
-                "launches_per_fwd": conv_n, "flops_per_launch": conv_fl / max(conv_n, 1),
-                "all_gemm_tflops": gemm_fl / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None,
-                "all_gemm_launches_per_fwd": gemm_n,
+                "launches_per_fwd": g_n, "flops_per_launch": g_fl / max(g_n, 1),
                 "whole_forward_tflops": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12,
                 "whole_forward_frac_of_sustained": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_sust,
-                "categories_ms": {k: round(v[0], 4) for k, v in prof.items()}}
-    gn = prof.get("GN")
-    if gn and gn[0] > 0:
-        roofline["groupnorm_gbs"] = gn[3] / (gn[0] / 1000.0) / 1e9
-        roofline["groupnorm_frac_of_hbm"] = roofline["groupnorm_gbs"] / hbm
+                "categories_replayed_alone_ms": {k: round(v[0], 4) for k, v in cats.items()},
+                "categories_launches": {k: v[1] for k, v in cats.items()}}
+    if "CONV3" in cats:
+        c_ms, c_n, c_fl, _ = cats["CONV3"]
+        roofline["conv3x3"] = {"tflops": c_fl / (c_ms / 1000.0) / 1e12, "frac": c_fl / (c_ms / 1000.0) / 1e12 / tc_burst,
+                               "launches_per_fwd": c_n, "ms_per_fwd": c_ms}
+    if "ATTN" in cats:
+        a_ms, a_n, a_fl, _ = cats["ATTN"]
+        roofline["attention"] = {"tflops": a_fl / (a_ms / 1000.0) / 1e12,
+                                 "frac": a_fl / (a_ms / 1000.0) / 1e12 / tc_burst, "launches_per_fwd": a_n}
+    for c, key in (("GN", "groupnorm"), ("LN", "layernorm")):
+        if c in cats and cats[c][0] > 0:
+            gbs = cats[c][3] / (cats[c][0] / 1000.0) / 1e9
+            roofline[key] = {"gbs": gbs, "frac_of_hbm": gbs / hbm, "launches_per_fwd": cats[c][1]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, sample = cpu_oracle_forward_rate(wts, threads)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    cfg3 = None
+    if not args.no_config3 and not args.wo8:
+        cfg3 = run_config3(eng, sdg, dev, world, rank)
 
     launches = eng.forward_launches(B, H, W)
     if rank == 0:
@@ -319,6 +410,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches * args.steps,
             "tensor_peak_frac": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_burst,
+            "config3_lcm": cfg3,
         }))
     eng.release()
     if world > 1:

@@ -146,6 +146,18 @@ SDG_API int sdg_lcm_denoise_ex(sdg_engine* e, const float* latents, const float*
  * status. */
 SDG_API int sdg_profile(sdg_engine* e, int B, int H, int W, sdg_profile_row* rows, int cap);
 
+/* No reference counterpart (measurement): device time of one op category of the
+ * forward at (B,H,W) without per-launch events. The forward's launches are recorded
+ * with their arguments; those of the named categories ("GN", "LN", "CONV3", "GEMM",
+ * "ATTN", "GEMV", "MISC"; several joined by ',' or '+') are captured alone, in forward
+ * order on one stream, as a CUDA graph that is replayed once to warm up and then
+ * `reps` times back to back between two CUDA events. *ms = mean time of one replay,
+ * i.e. that category's summed kernel time per forward; *launches = launches per
+ * replay; *flops / *bytes = the category's algorithmic work per forward. The replays
+ * overwrite the plan's intermediate buffers (the next forward recomputes them). */
+SDG_API int sdg_profile_category(sdg_engine* e, int B, int H, int W, const char* categories, int reps, double* ms,
+                                 int* launches, double* flops, double* bytes);
+
 /* Number of kernel launches of one forward at (B,H,W) (after a forward ran). */
 SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
 
@@ -154,6 +166,18 @@ SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
  * the current device: out4 = {tile width, CTA pair (0/1), workspace K splits, cluster
  * K splits}; with_workspace = 0 asks for the choice when no split-K workspace is given. */
 SDG_API int sdg_gemm_plan(int M, int N, int K, int taps, int with_workspace, int* out4);
+
+/* No reference counterpart (failure-path test; the reference has no device-side
+ * timeouts): runs the tensor-core GEMM y[M,N] = x[M,K] * w[N,K]^T on single-CTA
+ * 128x128 tiles with the pipeline stage of k-block iteration `stall_iter` (counted
+ * per CTA) never loaded, and every bounded wait limited to `wait_limit_us`. The
+ * waits on that stage expire, the kernel records a timeout code in `err_word`,
+ * waits for its own copies and MMAs in flight, frees its TMEM and returns. The call
+ * synchronises `stream`, clears the word and returns SDG_ERR_DEVICE naming the code
+ * (SDG_OK would mean nothing expired). Needs N % 128 == 0, K % 64 == 0 and more than
+ * stall_iter pipeline stages of K. No GPU fault, trap or hang is involved. */
+SDG_API int sdg_selftest_stalled_gemm(const uint16_t* x, const uint16_t* w, int M, int N, int K, uint16_t* y,
+                                      int stall_iter, int wait_limit_us, int* err_word, void* stream);
 
 /* --- operator surface (device pointers, fp16 NHWC, stream may be NULL) -------------
  * Replaces the engine's internal op wrappers conv / matmul / groupnorm(_silu) /

@@ -73,7 +73,10 @@ _SIGS = {
     "sdg_lcm_denoise_ex": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "sdg_profile": (_I, [_P, _I, _I, _I, ctypes.POINTER(ProfileRow), _I]),
     "sdg_forward_launches": (_I, [_P, _I, _I, _I]),
+    "sdg_profile_category": (_I, [_P, _I, _I, _I, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "sdg_gemm_plan": (_I, [_I, _I, _I, _I, _I, _P]),
+    "sdg_selftest_stalled_gemm": (_I, [_P, _P, _I, _I, _I, _P, _I, _I, _P, _P]),
     "sdg_conv2d": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P, _P, ctypes.c_size_t, _P,
                         _P]),
     "sdg_linear": (_I, [_P, _I, _I, _P, _P, _I, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
@@ -237,6 +240,15 @@ class Engine:
         if n < 0:
             raise SdgError(-n, last_error())
         return {rows[i].name.decode(): (rows[i].ms, rows[i].launches, rows[i].flops, rows[i].bytes) for i in range(n)}
+
+    def profile_category(self, categories: str, B: int = 2, H: int = 64, W: int = 64,
+                         reps: int = 20) -> Tuple[float, int, float, float]:
+        """(device ms per forward, launches per forward, algorithmic FLOPs, algorithmic bytes) of the
+        forward's launches of the given categories ("CONV3+GEMM", "GN", ...) replayed alone as a graph."""
+        ms, n, fl, by = ctypes.c_double(), _I(), ctypes.c_double(), ctypes.c_double()
+        check(lib().sdg_profile_category(self._h, B, H, W, categories.encode(), reps, ctypes.byref(ms),
+                                         ctypes.byref(n), ctypes.byref(fl), ctypes.byref(by)))
+        return ms.value, n.value, fl.value, by.value
 
     def forward_launches(self, B: int, H: int, W: int) -> int:
         return lib().sdg_forward_launches(self._h, B, H, W)

@@ -18,6 +18,12 @@ int op_fail(int code, const std::string& msg);
 
 // Load every "<key>.bin" of a reference weight directory (vk_engine.cpp:497-507:
 // raw fp16, no header). The engine validates sizes per key when it prepares.
+void sdg_internal_mark_file(sdg_engine* e, const char* key, const std::string& path);  // engine.cu
+
+// Reads every <key>.bin of `dir` (the reference's unet_w/ format: raw little-endian fp16, Linear
+// weights stored [in,out]; vk_engine.cpp:497-507). An unreadable, empty or odd-sized file is an I/O
+// error naming it; a file whose value count does not match its key is reported by sdg_prepare as
+// SDG_ERR_IO naming the file and the key (the reference instead substitutes zeros, :500-503).
 int sdg_internal_load_dir(sdg_engine* e, const char* dir) {
   DIR* d = opendir(dir);
   if (!d) return sdg::op_fail(SDG_ERR_IO, std::string("cannot open weight dir ") + dir);
@@ -32,14 +38,20 @@ int sdg_internal_load_dir(sdg_engine* e, const char* dir) {
     fseek(f, 0, SEEK_END);
     const long sz = ftell(f);
     fseek(f, 0, SEEK_SET);
-    if (sz <= 0 || sz % 2) { fclose(f); continue; }
+    if (sz <= 0 || sz % 2) {
+      fclose(f);
+      closedir(d);
+      return sdg::op_fail(SDG_ERR_IO, path + ": " + std::to_string(sz) + " bytes is not a whole number of fp16 values");
+    }
     buf.resize((size_t)sz / 2);
     const size_t got = fread(buf.data(), 2, buf.size(), f);
     fclose(f);
     if (got != buf.size()) { closedir(d); return sdg::op_fail(SDG_ERR_IO, "short read " + path); }
     const int64_t shape[1] = {(int64_t)buf.size()};
-    const int st = sdg_upload_weight(e, name.substr(0, name.size() - 4).c_str(), buf.data(), shape, 1);
+    const std::string key = name.substr(0, name.size() - 4);
+    const int st = sdg_upload_weight(e, key.c_str(), buf.data(), shape, 1);
     if (st) { closedir(d); return st; }
+    sdg_internal_mark_file(e, key.c_str(), path);
     ++n;
   }
   closedir(d);
@@ -142,6 +154,36 @@ static int linear_common(const char* name, const uint16_t* x, int M, int K, cons
   return cuda_status(sdg::launch_gemm(a, err, static_cast<cudaStream_t>(stream)), name);
 }
 
+SDG_API int sdg_selftest_stalled_gemm(const uint16_t* x, const uint16_t* w, int M, int N, int K, uint16_t* y,
+                                      int stall_iter, int wait_limit_us, int* err_word, void* stream) {
+  if (!x || !w || !y || !err_word || M <= 0 || N <= 0 || N % 128 || K <= 0 || K % 64 || stall_iter < 0 ||
+      wait_limit_us <= 0 || wait_limit_us > 2000000)
+    return sdg::op_fail(SDG_ERR_ARG, "selftest_stalled_gemm: bad arguments");
+  sdg::GemmArgs a;
+  a.M = M; a.N = N; a.K = K; a.taps = 1;
+  a.a0 = reinterpret_cast<const __half*>(x); a.cin0 = K;
+  a.w = reinterpret_cast<const __half*>(w);
+  a.out = reinterpret_cast<__half*>(y);
+  a.bn = 128;  // single-CTA 128x128 tiles, no K split: one pipeline per CTA
+  a.test_stall_iter = stall_iter;
+  a.wait_limit_ns = 1000ull * (unsigned long long)wait_limit_us;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = cuda_status(sdg::launch_gemm(a, err_word, s), "selftest_stalled_gemm");
+  if (st) return st;
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, err_word, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "selftest_stalled_gemm");
+  if (v != 0) {
+    cudaMemsetAsync(err_word, 0, sizeof(int), s);
+    cudaStreamSynchronize(s);
+    char buf[112];
+    snprintf(buf, sizeof buf, "selftest_stalled_gemm: device error word 0x%x (a kernel's bounded wait expired)", v);
+    return sdg::op_fail(SDG_ERR_DEVICE, buf);
+  }
+  return SDG_OK;
+}
+
 SDG_API int sdg_gemm_plan(int M, int N, int K, int taps, int with_workspace, int* out4) {
   if (!out4 || M <= 0 || N <= 0 || K <= 0 || K % 64 || !(taps == 1 || taps == 9) || K % (64 * taps))
     return sdg::op_fail(SDG_ERR_ARG, "gemm_plan: bad arguments");
@@ -171,7 +213,8 @@ SDG_API int sdg_linear_wo8(const uint16_t* x, int M, int K, const int8_t* w8, co
 SDG_API int sdg_groupnorm(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,
                           const float* gamma, const float* beta, float eps, int silu, uint16_t* y,
                           float* stats_scratch, void* stream) {
-  if (!x || !y || !gamma || !beta || !stats_scratch || (x2 == nullptr) != (C2 == 0))
+  if (!x || !y || !gamma || !beta || !stats_scratch || (x2 == nullptr) != (C2 == 0) || B <= 0 || HW <= 0 ||
+      C1 <= 0 || C2 < 0 || groups <= 0)
     return sdg::op_fail(SDG_ERR_ARG, "groupnorm: bad arguments");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   sdg::GroupNormArgs a;

@@ -207,9 +207,9 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
           tma_load_3d(smem_u32(sV + s * CF::kVTile + a * CF::kVAtom), &map_v, kv_full(s), j * BKV + 64 * a, 0, bh);
       }
       if (!ok) {
-        mbar_wait(q_full, 0, p.err, kDevTimeoutDrain);
+        mbar_drain(q_full, 0, p.err, kDevTimeoutDrain);
         for (int s = 0; s < NKV; ++s)
-          if (issued[s]) mbar_wait(kv_full(s), (uint32_t)last_ph[s], p.err, kDevTimeoutDrain);
+          if (issued[s]) mbar_drain(kv_full(s), (uint32_t)last_ph[s], p.err, kDevTimeoutDrain);
       }
     }
   } else if (warp == 1) {
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         }
       }
       mma_commit(drain);
-      mbar_wait(drain, 0, p.err, kDevTimeoutDrain);
+      mbar_drain(drain, 0, p.err, kDevTimeoutDrain);
     }
   } else if constexpr (CF::TPV) {
     // ---------------------------------------------------------------- softmax, transposed PV

@@ -18,6 +18,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 #include <string>
@@ -52,6 +53,7 @@ static const int kCtxPad = 80;  // cross-attention V^T row length (77 keys, padd
 struct HostWeight {
   std::vector<uint16_t> data;
   std::vector<int64_t> shape;
+  std::string file;  // the <key>.bin it was read from (sdg_load_dir), empty when uploaded from memory
 };
 // fp16 weights (w), or weight-only int8 (w8 + per-row scale ws) after sdg_quantize_wo8
 struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; int8_t* w8 = nullptr; float* ws = nullptr; };
@@ -127,6 +129,9 @@ class Builder {
   // K/V projections (their outputs persist in the arena between runs of the same plan)
   bool ctx_cached = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof;
+  // recording: every launch of the forward with its arguments, in issue order (replayed per
+  // category by sdg_profile_category to time one kind of kernel alone)
+  std::vector<std::pair<int, std::function<cudaError_t(cudaStream_t)>>>* rec = nullptr;
   double cat_flops[8] = {0}, cat_bytes[8] = {0};  // algorithmic work per category (counted in every mode)
 
  private:
@@ -192,6 +197,13 @@ class Builder {
   bool ok() const { return status_ == SDG_OK; }
   void check(cudaError_t err, const char* what, int cat, int nk = 1);
   void begin_op(int cat);
+  // One launch (nk kernels) of category `cat`: `f(stream)` issues it on s_, recorded when recording.
+  template <typename F>
+  void issue(int cat, const char* what, int nk, F f) {
+    begin_op(cat);
+    if (rec) rec->push_back({cat, std::function<cudaError_t(cudaStream_t)>(f)});
+    check(f(s_), what, cat, nk);
+  }
   cudaEvent_t ev_start_ = nullptr;
 
   // ops
@@ -246,6 +258,7 @@ struct WeightPacker {
   };
   std::vector<Mat> mats;
   std::string missing;
+  std::string io_error;  // a weight read from a file holds the wrong number of values
   explicit WeightPacker(Engine& en) : e(en) {}
   // Register the matrix at `off`; reserves its per-row scale array (used by wo8).
   void mat(size_t off, int rows, int cols, __half** w16, int8_t** w8, float** ws) {
@@ -285,7 +298,14 @@ struct WeightPacker {
   const HostWeight* get(const std::string& k, size_t numel) {
     auto it = e.host.find(k);
     if (it == e.host.end() || it->second.data.size() != numel) {
-      if (missing.empty()) missing = k + (it == e.host.end() ? " (missing)" : " (wrong size)");
+      if (it != e.host.end() && !it->second.file.empty()) {
+        if (io_error.empty())
+          io_error = "weight file " + it->second.file + " for " + k + " holds " +
+                     std::to_string(it->second.data.size()) + " fp16 values, expected " + std::to_string(numel) +
+                     " (truncated or not this key's tensor)";
+      } else if (missing.empty()) {
+        missing = k + (it == e.host.end() ? " (missing)" : " (wrong size)");
+      }
       return nullptr;
     }
     return &it->second;
@@ -504,6 +524,7 @@ int Engine::prepare() {
       for (int c = 0; c < pr.second->cout; ++c) bd[pr.second->tp_off + c] = hb ? h2f(hb->data[c]) : 0.f;
     }
   }
+  if (!P.io_error.empty()) return fail(SDG_ERR_IO, P.io_error);
   if (!P.missing.empty()) return fail(SDG_ERR_MISSING_WEIGHT, "weight " + P.missing);
   if (wo8) P.quantize_wo8();
   SDG_CUDA_TRY(cudaSetDevice(device));
@@ -565,8 +586,7 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
   if (dry_ || !ok()) { launches_ += groupnorm_launch_count(a); return; }
-  begin_op(kCatGN);
-  check(launch_groupnorm(a, s_), "groupnorm", kCatGN, groupnorm_launch_count(a));
+  issue(kCatGN, "groupnorm", groupnorm_launch_count(a), [a](cudaStream_t s) { return launch_groupnorm(a, s); });
 }
 
 void Builder::gemm(GemmArgs a, int cat) {
@@ -579,8 +599,8 @@ void Builder::gemm(GemmArgs a, int cat) {
     off_ = mark;
     return;
   }
-  begin_op(cat);
-  check(launch_gemm(a, pl_.dev_err, s_), cat == kCatConv3 ? "conv3x3" : "gemm", cat, gemm_launch_count(a));
+  issue(cat, cat == kCatConv3 ? "conv3x3" : "gemm", gemm_launch_count(a),
+        [a, err = pl_.dev_err](cudaStream_t s) { return launch_gemm(a, err, s); });
   off_ = mark;
 }
 
@@ -682,8 +702,9 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   auto ln = [&](const __half* xin, const Norm& n) {
     cat_bytes[kCatLN] += 2.0 * 2.0 * M * C;
     if (dry_ || !ok()) { launches_++; return; }
-    begin_op(kCatLN);
-    check(launch_layernorm(xin, M, C, n.g, n.b, kLnEps, hn, s_), "layernorm", kCatLN);
+    issue(kCatLN, "layernorm", 1, [=, g = n.g, b = n.b](cudaStream_t s) {
+      return launch_layernorm(xin, M, C, g, b, kLnEps, hn, s);
+    });
   };
   auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
                    int vt_idx, int spad) {
@@ -701,8 +722,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
     AttnArgs a;
     a.q = q; a.k = k; a.v = vt; a.BH = B * kHeads; a.heads = kHeads; a.Sq = S; a.Sk = Sk; a.d = d; a.dp = dp;
     a.d16 = d16; a.vt_ld = vt_ld; a.o = o; a.ld_o = C; a.scale = 1.0f / sqrtf((float)d);
-    begin_op(kCatAttn);
-    check(launch_attention(a, pl_.dev_err, s_), "attention", kCatAttn);
+    issue(kCatAttn, "attention", 1, [a, err = pl_.dev_err](cudaStream_t s) { return launch_attention(a, err, s); });
   };
   lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
   ln(tt, t.ln1);
@@ -739,8 +759,9 @@ Buf Builder::downsample(const ConvW& c, const Buf& x, int H, int W) {
   const size_t mark = off_;
   __half* col = alloc_h((size_t)M * 9 * x.C);
   if (!dry_ && ok()) {
-    begin_op(kCatMisc);
-    check(launch_im2col3x3(x.p, B, H, W, x.C, 2, 9 * x.C, col, s_), "im2col", kCatMisc);
+    issue(kCatMisc, "im2col", 1, [=, xp = x.p, C = x.C](cudaStream_t s) {
+      return launch_im2col3x3(xp, B, H, W, C, 2, 9 * C, col, s);
+    });
   } else {
     launches_++;
   }
@@ -758,8 +779,9 @@ Buf Builder::upsample(const ConvW& c, const Buf& x, int H, int W) {
   const size_t mark = off_;
   __half* up = alloc_h((size_t)M * x.C);
   if (!dry_ && ok()) {
-    begin_op(kCatMisc);
-    check(launch_upsample2x(x.p, B, H, W, x.C, up, s_), "upsample", kCatMisc);
+    issue(kCatMisc, "upsample", 1, [=, xp = x.p, C = x.C](cudaStream_t s) {
+      return launch_upsample2x(xp, B, H, W, C, up, s);
+    });
   } else {
     launches_++;
   }
@@ -801,22 +823,26 @@ int Builder::run() {
   (void)persistent_end;
 
   if (!dry_) temb_ready_ = on_side([&] {  // time embedding + projections: needed first by the first conv1
-    begin_op(kCatMisc);
-    check(launch_time_embedding(pl_.t_in, B, B, pl_.mode == 1 ? pl_.tproj_in : nullptr, te, s_), "time_embedding", kCatMisc);
-    begin_op(kCatGemv);
-    check(launch_gemv(te, B, 320, w.t1.w, w.t1.w8, w.t1.ws, w.t1.b, kTemb, 0, 1, t1, kTemb, s_), "time mlp 1",
-          kCatGemv, (B + 7) / 8);
-    begin_op(kCatGemv);
+    const float* tproj = pl_.mode == 1 ? pl_.tproj_in : nullptr;
+    issue(kCatMisc, "time_embedding", 1, [=, tin = pl_.t_in](cudaStream_t s) {
+      return launch_time_embedding(tin, B, B, tproj, te, s);
+    });
+    const int ngv = (B + 7) / 8;
+    issue(kCatGemv, "time mlp 1", ngv, [=, L = w.t1](cudaStream_t s) {
+      return launch_gemv(te, B, 320, L.w, L.w8, L.ws, L.b, kTemb, 0, 1, t1, kTemb, s);
+    });
     // temb's only consumers are the time_emb_proj of every ResNet, each after SiLU: apply it once here
-    check(launch_gemv(t1, B, kTemb, w.t2.w, w.t2.w8, w.t2.ws, w.t2.b, kTemb, 0, 1, temb, kTemb, s_), "time mlp 2",
-          kCatGemv, (B + 7) / 8);
-    begin_op(kCatGemv);
-    check(launch_gemv(temb, B, kTemb, w.tp_w, w.tp_w8, w.tp_ws, w.tp_b, w.tp_N, 0, 0, tp_all_, w.tp_N, s_),
-          "time_emb_proj", kCatGemv, (B + 7) / 8);
-    if (!ctx_cached) {
-      begin_op(kCatMisc);
-      check(launch_f32_to_f16(pl_.ctx_in, (size_t)B * kCtxLen * kCtxDim, ctx16_, s_), "ctx f16", kCatMisc);
-    }
+    issue(kCatGemv, "time mlp 2", ngv, [=, L = w.t2](cudaStream_t s) {
+      return launch_gemv(t1, B, kTemb, L.w, L.w8, L.ws, L.b, kTemb, 0, 1, temb, kTemb, s);
+    });
+    issue(kCatGemv, "time_emb_proj", ngv, [=, tpw = w.tp_w, tpw8 = w.tp_w8, tpws = w.tp_ws, tpb = w.tp_b, tpN = w.tp_N,
+                                           tpa = tp_all_](cudaStream_t s) {
+      return launch_gemv(temb, B, kTemb, tpw, tpw8, tpws, tpb, tpN, 0, 0, tpa, tpN, s);
+    });
+    if (!ctx_cached)
+      issue(kCatMisc, "ctx f16", 1, [=, cin = pl_.ctx_in, c16 = ctx16_](cudaStream_t s) {
+        return launch_f32_to_f16(cin, (size_t)B * kCtxLen * kCtxDim, c16, s);
+      });
   });
   else
     launches_ += 3 + 3 * ((B + 7) / 8);
@@ -839,8 +865,9 @@ int Builder::run() {
     const size_t mark = off_;
     __half* col = alloc_h((size_t)M * 64);
     if (!dry_ && ok()) {
-      begin_op(kCatMisc);
-      check(launch_latent_im2col(pl_.lat_in, B, 4, H, W, 64, col, s_), "latent im2col", kCatMisc);
+      issue(kCatMisc, "latent im2col", 1, [=, lat = pl_.lat_in](cudaStream_t s) {
+        return launch_latent_im2col(lat, B, 4, H, W, 64, col, s);
+      });
     } else {
       launches_++;
     }
@@ -1018,6 +1045,13 @@ struct sdg_engine {
 };
 
 int sdg_internal_load_dir(sdg_engine* e, const char* dir);  // api_ops.cu
+
+// Records the file a weight was read from, so a file of the wrong size is reported as an I/O error.
+void sdg_internal_mark_file(sdg_engine* h, const char* key, const std::string& path) {
+  auto it = h->e.host.find(key);
+  if (it != h->e.host.end()) it->second.file = path;
+}
+
 
 static const double kHostDeadlineS = 60.0;
 
@@ -1339,6 +1373,87 @@ SDG_API int sdg_profile(sdg_engine* h, int B, int H, int W, sdg_profile_row* row
     ++n;
   }
   return n;
+}
+
+SDG_API int sdg_profile_category(sdg_engine* h, int B, int H, int W, const char* categories, int reps, double* ms,
+                                 int* launches, double* flops, double* bytes) {
+  if (!h) return SDG_ERR_NOT_INIT;
+  if (!categories || reps <= 0 || !ms) return fail(SDG_ERR_ARG, "profile_category: bad arguments");
+  bool want[sdg::kCatCount] = {false};
+  {
+    std::string list(categories);
+    size_t pos = 0;
+    while (pos <= list.size()) {
+      size_t end = list.find_first_of(",+", pos);
+      if (end == std::string::npos) end = list.size();
+      const std::string name = list.substr(pos, end - pos);
+      int c = 0;
+      while (c < sdg::kCatCount && name != sdg::kCatName[c]) ++c;
+      if (c == sdg::kCatCount) return fail(SDG_ERR_ARG, "profile_category: unknown category '" + name + "'");
+      want[c] = true;
+      pos = end + 1;
+    }
+  }
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return st;
+  // 1) record the forward's launches with their arguments (captured, never launched)
+  std::vector<std::pair<int, std::function<cudaError_t(cudaStream_t)>>> rec;
+  sdg::Builder b(e, *p, false, e.stream);
+  b.rec = &rec;
+  if (cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return fail(SDG_ERR_CUDA, "profile_category: capture");
+  st = b.run();
+  cudaGraph_t g0 = nullptr;
+  const cudaError_t ce0 = cudaStreamEndCapture(e.stream, &g0);
+  if (g0) cudaGraphDestroy(g0);
+  if (st != SDG_OK) return st;
+  if (ce0 != cudaSuccess) return fail(SDG_ERR_CUDA, std::string("profile_category: ") + cudaGetErrorString(ce0));
+  // 2) the selected launches alone, in forward order on one stream, as one graph
+  int n = 0;
+  if (cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return fail(SDG_ERR_CUDA, "profile_category: capture");
+  cudaError_t le = cudaSuccess;
+  for (auto& r : rec)
+    if (want[r.first]) {
+      const cudaError_t x = r.second(e.stream);
+      if (x != cudaSuccess && le == cudaSuccess) le = x;
+      ++n;
+    }
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t gx = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(e.stream, &g);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  bool ok = le == cudaSuccess && ce == cudaSuccess && n > 0 && cudaGraphInstantiate(&gx, g, 0) == cudaSuccess &&
+            cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+  // 3) one warm-up replay, then `reps` replays back to back between two events
+  ok = ok && cudaGraphLaunch(gx, e.stream) == cudaSuccess && cudaEventRecord(e0, e.stream) == cudaSuccess;
+  for (int i = 0; ok && i < reps; ++i) ok = cudaGraphLaunch(gx, e.stream) == cudaSuccess;
+  ok = ok && cudaEventRecord(e1, e.stream) == cudaSuccess;
+  ok = cudaStreamSynchronize(e.stream) == cudaSuccess && ok;
+  float t = 0.f;
+  if (ok) ok = cudaEventElapsedTime(&t, e0, e1) == cudaSuccess;
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (gx) cudaGraphExecDestroy(gx);
+  if (g) cudaGraphDestroy(g);
+  if (!ok) {
+    cudaGetLastError();
+    return fail(n == 0 ? SDG_ERR_ARG : SDG_ERR_CUDA, n == 0 ? "profile_category: no launch of that category"
+                                                             : "profile_category: replay failed");
+  }
+  const int dev_status = e.check_dev_err(p, e.stream);
+  if (dev_status) return dev_status;
+  *ms = (double)t / reps;
+  double fl = 0, by = 0;
+  for (int c = 0; c < sdg::kCatCount; ++c)
+    if (want[c]) { fl += b.cat_flops[c]; by += b.cat_bytes[c]; }
+  if (launches) *launches = n;
+  if (flops) *flops = fl;
+  if (bytes) *bytes = by;
+  return SDG_OK;
 }
 
 }  // extern "C"

@@ -10,8 +10,10 @@
 //               from TMEM, fused bias / per-image bias / residual / SiLU /
 //               GEGLU / head scatter, fp16 stores
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps
-// the main loop of tile i+1. No cluster multicast is used anywhere. A CTA pair
-// (cluster of 2, tcgen05.mma.cta_group::2) computes 256-row tiles.
+// the main loop of tile i+1. No TMA load uses multicast (the only
+// .multicast::cluster is the tcgen05.commit that signals an mbarrier in both
+// CTAs of a pair). A CTA pair (cluster of 2, tcgen05.mma.cta_group::2)
+// computes 256-row tiles.
 //
 // Weight-only int8 (wo8): W arrives as int8 by TMA into a staging tile;
 // 4 converter warps (warps 6..9, leaving warps 2..5 to the epilogue) rewrite
@@ -67,6 +69,8 @@ struct GemmDev {
   float* ws;                 // [splits][M][N] fp32 partials when splits > 1
   const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
+  int stall_it;              // failure-path test: k-block iteration whose stage is never loaded (-1: none)
+  unsigned long long wait_ns;  // limit of every bounded wait
 };
 
 // PAIR: a CTA pair (cluster of 2) computes a 256 x BN tile with
@@ -406,7 +410,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           const int nsub = min(G, kb1 - kb);  // k-blocks in this stage (the unit's last may be short)
-          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty, p.wait_ns)) { ok = false; break; }
+          if ((int)it == p.stall_it) continue;  // failure-path test: this stage is never loaded
           if (rank == 0) mbar_arrive_expect_tx(full_bar(s), (uint32_t)nsub * C::kTxBytes);
           issued[s] = true;
           last_phase[s] = ph;
@@ -448,7 +453,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         // CTA of a pair cannot observe the even CTA's barrier and waits out a fixed time
         if (rank == 0) {
           for (int s = 0; s < S; ++s)
-            if (issued[s]) mbar_wait(full_bar(s), (uint32_t)last_phase[s], p.err, kDevTimeoutDrain);
+            if (issued[s]) mbar_drain(full_bar(s), (uint32_t)last_phase[s], p.err, kDevTimeoutDrain, p.wait_ns);
         } else {
           spin_ns(200000);
         }
@@ -464,8 +469,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         int m_blk, n_blk, kb0, kb1;
         decode(unit, m_blk, n_blk, kb0, kb1);
         const uint32_t acc = tl & 1u, acc_ph = (tl >> 1) & 1u;
-        const bool got = PAIR ? mbar_wait_cluster(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc)
-                              : mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc);
+        const bool got = PAIR ? mbar_wait_cluster(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc, p.wait_ns)
+                              : mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.err, kDevTimeoutAcc, p.wait_ns);
         if (!got) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
@@ -473,8 +478,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
           const int nsub = min(G, kb1 - kb);
-          if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
-          if (W8 && !mbar_wait(conv_bar(s), ph, p.err, kDevTimeoutFull)) { ok = false; break; }
+          if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull, p.wait_ns)) { ok = false; break; }
+          if (W8 && !mbar_wait(conv_bar(s), ph, p.err, kDevTimeoutFull, p.wait_ns)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int g = 0; g < G; ++g) {
@@ -508,7 +513,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         mma_commit2_mc(drain_bar, 0x1);
       else
         mma_commit(drain_bar);
-      mbar_wait(drain_bar, 0, p.err, kDevTimeoutDrain);
+      mbar_drain(drain_bar, 0, p.err, kDevTimeoutDrain, p.wait_ns);
     }
   } else if (W8 && warp >= 6) {
     // ------------------------------------------------------------ int8 -> fp16 converters (wo8)
@@ -521,7 +526,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % S;
         const uint32_t ph = (it / S) & 1u;
-        ok = mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull);
+        ok = mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull, p.wait_ns);
         if (!ok) break;
         const uint8_t* src = sB8 + s * C::kB8Bytes;
         uint8_t* dst = sB + s * C::kBTileBytes;
@@ -559,7 +564,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
       if (p.splits == 1 && csp == 1 && p.epi != kEpiGeglu) epi_prefetch<C::kChunk>(p, m, img, n0 + eh * C::kChunk, mvalid);
-      bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc);
+      bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc, p.wait_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
@@ -840,13 +845,19 @@ constexpr TileCost kTileCosts[] = {
 constexpr double kCsplitUs = 0.92, kCsplitUsPerCta = 0.62, kCsplitUsPer128Cols = 0.61;
 
 // Clusters of `cs` GEMM CTAs (one CTA per SM) that can be resident at once: a cluster must fit in
-// one GPC, so this is below num_sms() / cs for the larger sizes.
+// one GPC, so this is below num_sms() / cs for the larger sizes. 0 when the device answers that no
+// such cluster fits (the chooser then skips that split). Without a device (plan queries on a host
+// with no GPU) the estimate is num_sms() / cs.
 int cluster_capacity(int cs) {
   static int cap[64][kMaxCsplitCtas + 1] = {};
+  static bool known[64][kMaxCsplitCtas + 1] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
   if (dev >= 64 || cs < 2 || cs > kMaxCsplitCtas) return std::max(1, num_sms() / std::max(1, cs));
-  if (!cap[dev][cs]) {
+  if (!known[dev][cs]) {
     using C = Cfg<160, false, false>;
     auto k = gemm_tc_kernel<160, false, false>;
     int n = 0;
@@ -862,10 +873,13 @@ int cluster_capacity(int cs) {
       at[0].val.clusterDim.z = 1;
       cfg.attrs = at;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) != cudaSuccess) n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) != cudaSuccess) n = -1;
+    } else {
+      n = -1;  // no device to ask
     }
     cudaGetLastError();
-    cap[dev][cs] = n > 0 ? n : std::max(1, num_sms() / cs);
+    cap[dev][cs] = n >= 0 ? n : std::max(1, num_sms() / cs);
+    known[dev][cs] = true;
   }
   return cap[dev][cs];
 }
@@ -909,6 +923,7 @@ TileChoice choose_tiles(const GemmArgs& a, bool allow_ws = true) {
       }
       if (sp == 1 || (!tcst.pair && sp <= kMaxCsplitCtas)) {  // single pass, or cluster split-K
         const int cap = sp > 1 ? cluster_capacity(sp) : teams;  // resident clusters (sp > 1) or CTAs
+        if (cap <= 0) continue;                                  // no cluster of this size fits
         const int waves = (tiles + cap - 1) / cap;
         double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit);
         if (sp > 1) t += kCsplitUs + kCsplitUsPerCta * sp + kCsplitUsPer128Cols * bn / 128.0;
@@ -977,6 +992,8 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.csplit = tc.csplit;
   d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
+  d.stall_it = a.test_stall_iter;
+  d.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kWaitTimeoutNs;
   if (a.w8 && !a.wscale) return cudaErrorInvalidValue;
   // the epilogue reads bias / per-image bias 8 columns at a time as two float4
   if ((reinterpret_cast<uintptr_t>(a.bias) | reinterpret_cast<uintptr_t>(a.rowbias)) & 15) return cudaErrorInvalidValue;

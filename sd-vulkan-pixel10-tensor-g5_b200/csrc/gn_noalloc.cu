@@ -1,7 +1,8 @@
 // gn_noalloc.cu — GroupNorm entry point that allocates nothing.
 //
-// sdg_groupnorm needs a few hundred KB of device scratch for its per-chunk
-// statistics, and expects the caller to pass it. Some callers have no way to
+// sdg_groupnorm needs device scratch for its statistics, one (mean, rstd)
+// pair of floats per (image, group), i.e. B * groups * 8 bytes, and expects
+// the caller to pass it. Some callers have no way to
 // allocate device memory: a Kotlin/JNI or other foreign-language front end
 // that reaches this library only through its C ABI and links no CUDA runtime
 // of its own, or a host process whose device memory is owned by another
@@ -61,7 +62,8 @@ SDG_API size_t sdg_groupnorm_noalloc_max_scratch_bytes(void) { return kNoAllocSc
 SDG_API int sdg_groupnorm_noalloc(const uint16_t* x, const uint16_t* x2, int B, int HW, int C1, int C2, int groups,
                                   const float* gamma, const float* beta, float eps, int silu, uint16_t* y,
                                   void* stream) {
-  if (!x || !y || !gamma || !beta || (x2 == nullptr) != (C2 == 0) || B <= 0 || HW <= 0 || C1 <= 0 || groups <= 0)
+  if (!x || !y || !gamma || !beta || (x2 == nullptr) != (C2 == 0) || B <= 0 || HW <= 0 || C1 <= 0 || C2 < 0 ||
+      groups <= 0)
     return sdg::op_fail(SDG_ERR_ARG, "groupnorm_noalloc: bad arguments");
   const size_t need = sdg::groupnorm_scratch_bytes(B, HW, C1 + C2, groups);
   if (need > kNoAllocScratchBytes)

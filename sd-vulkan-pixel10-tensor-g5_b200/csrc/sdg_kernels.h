@@ -52,6 +52,10 @@ struct GemmArgs {
   int bn = 0;                       // tile N (0 = choose)
   float* ws = nullptr;              // split-K workspace (fp32); split-K only when large enough
   size_t ws_bytes = 0;
+  // Failure-path test only (sdg_selftest_stalled_gemm): the producer leaves the pipeline stage of this
+  // k-block iteration (counted per CTA) unloaded, so the waits on it expire after wait_limit_ns.
+  int test_stall_iter = -1;
+  unsigned long long wait_limit_ns = 0;  // 0: the default 2 s limit of every bounded wait
 };
 
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s);

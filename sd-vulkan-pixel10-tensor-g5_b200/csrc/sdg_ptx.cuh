@@ -1,6 +1,8 @@
 // sdg_ptx.cuh — thin inline-PTX layer for sm_100a: mbarriers with bounded
-// waits, TMA tensor loads (no multicast anywhere), tcgen05 (TMEM alloc, MMA,
-// commit, loads) and shared-memory matrix descriptors.
+// waits, TMA tensor loads, tcgen05 (TMEM alloc, MMA, commit, loads) and
+// shared-memory matrix descriptors. No TMA or bulk load uses multicast; the
+// only .multicast::cluster here is tcgen05.commit's mbarrier arrive on the
+// two CTAs of a pair (a completion signal, not a data load).
 //
 // Every spin-wait is bounded by a wall-clock deadline (%globaltimer). On
 // expiry the waiting thread records an error code in the kernel's error word
@@ -80,19 +82,36 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for the phase with parity `parity` to complete. Returns false
-// (after recording `code`) when the deadline passes or another thread of the
+// (after recording `code`) when `limit_ns` passes or another thread of the
 // launch has already failed.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         return false;
       }
+    }
+  }
+}
+// Abort-path wait for work this thread put in flight (TMA copies, MMAs) before
+// the shared memory or TMEM they target is released. Unlike mbar_wait it keeps
+// waiting after another thread has recorded an error (that is why the kernel is
+// aborting); it gives up only after `limit_ns`, recording `code`.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, int* err, int code,
+                                           uint64_t limit_ns = kWaitTimeoutNs) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u && globaltimer() - t0 > limit_ns) {
+      atomicCAS(err, 0, code);
+      return false;
     }
   }
 }
@@ -166,14 +185,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   return ok != 0;
 }
 // Bounded wait with cluster-scope acquire (arrivals come from the peer CTA too).
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code,
+                                                  uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         return false;
       }

@@ -51,25 +51,32 @@ def gather_latents(local: "np.ndarray", n_total: int, group=None, device=None) -
 
 def lcm_generate(denoise: Callable[..., "np.ndarray"], latents: "np.ndarray", cond: "np.ndarray",
                  uncond: "np.ndarray", step_noise: Optional["np.ndarray"], steps: int = 4, cfg: float = 1.5,
-                 group=None, device=None, chunk: int = 32) -> "np.ndarray":
+                 group=None, device=None, chunk: int = 32, timings: Optional[dict] = None) -> "np.ndarray":
     """Denoise this rank's shard of the batch and gather every image's final latent.
 
     ``denoise(latents, cond, uncond, step_noise, steps=, cfg=)`` is normally
     ``Engine.lcm_denoise`` (which takes at most 32 images per call; larger
     shards are processed in chunks). ``latents``/``cond``/``uncond`` hold the
     whole batch; ``step_noise`` is [steps-1, n, 4, H, W] (host-generated per
-    image so every rank count yields identical results)."""
+    image so every rank count yields identical results). When ``timings`` is
+    a dict it receives this rank's host wall-clock seconds of the denoise
+    (``denoise_s``) and of the gather (``gather_s``)."""
+    import time
     import torch.distributed as dist
     n = latents.shape[0]
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     s, c = shard(n, world, rank)
+    t0 = time.perf_counter()
     outs = []
     for a in range(s, s + c, chunk):
         b = min(s + c, a + chunk)
         nz = None if step_noise is None else np.ascontiguousarray(step_noise[:, a:b])
         outs.append(denoise(latents[a:b], cond[a:b], uncond[a:b], nz, steps=steps, cfg=cfg))
     local = np.concatenate(outs, 0) if outs else np.zeros((0,) + latents.shape[1:], np.float32)
-    if world == 1:
-        return local
-    return gather_latents(local, n, group=group, device=device)
+    t1 = time.perf_counter()
+    out = local if world == 1 else gather_latents(local, n, group=group, device=device)
+    if timings is not None:
+        timings["denoise_s"] = t1 - t0
+        timings["gather_s"] = time.perf_counter() - t1
+    return out

@@ -1,5 +1,9 @@
-"""Host logic of the GEMM tile chooser, through ``sdg_gemm_plan`` (no kernel runs, no GPU needed:
-without a device the chooser uses 148 SMs and num_sms / cluster-size resident clusters).
+"""Host logic of the GEMM tile chooser, through ``sdg_gemm_plan`` (no kernel runs, no GPU needed).
+
+The plans depend on the device: without one the chooser assumes 148 SMs and num_sms / cluster-size
+resident clusters; with one it asks the device how many clusters of each size fit
+(cudaOccupancyMaxActiveClusters), so a plan checked here on a host without a GPU can differ from the
+one a B200 runs. The invariants below hold either way.
 
 Invariants the kernels rely on: the tile width divides N (or is the ragged 64 fallback), a K split
 is either a workspace split or a cluster split of at most 8 CTAs (never both, never on a CTA pair),
