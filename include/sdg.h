@@ -158,6 +158,22 @@ SDG_API int sdg_profile(sdg_engine* e, int B, int H, int W, sdg_profile_row* row
 SDG_API int sdg_profile_category(sdg_engine* e, int B, int H, int W, const char* categories, int reps, double* ms,
                                  int* launches, double* flops, double* bytes);
 
+typedef struct sdg_launch_row {
+  char label[128];  /* op, shape and (GEMMs) the tile chooser's plan */
+  char category[8]; /* GN, LN, CONV3, GEMM, ATTN, GEMV, MISC */
+  double ms;        /* device time of this launch (see sdg_profile_launches) */
+  double flops;     /* algorithmic FLOPs of the launch */
+  double bytes;     /* algorithmic HBM bytes of the launch (norms) */
+} sdg_launch_row;
+
+/* No reference counterpart (measurement): per-launch device times of the forward's
+ * launches of the named categories (as for sdg_profile_category), in forward order:
+ * each launch is captured `reps` times back to back in a CUDA graph with its recorded
+ * arguments, replayed once after a warm-up replay; ms = replay time / reps. Returns
+ * the number of rows written (<= cap) or a negative status. */
+SDG_API int sdg_profile_launches(sdg_engine* e, int B, int H, int W, const char* categories, int reps,
+                                 sdg_launch_row* rows, int cap);
+
 /* Number of kernel launches of one forward at (B,H,W) (after a forward ran). */
 SDG_API int sdg_forward_launches(sdg_engine* e, int B, int H, int W);
 

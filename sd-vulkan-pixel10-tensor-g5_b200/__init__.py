@@ -47,6 +47,11 @@ class SdgError(RuntimeError):
         self.code = code
 
 
+class LaunchRow(ctypes.Structure):
+    _fields_ = [("label", ctypes.c_char * 128), ("category", ctypes.c_char * 8), ("ms", ctypes.c_double),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
 class ProfileRow(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 32), ("ms", ctypes.c_double), ("launches", ctypes.c_int),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -73,6 +78,7 @@ _SIGS = {
     "sdg_lcm_denoise_ex": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P]),
     "sdg_profile": (_I, [_P, _I, _I, _I, ctypes.POINTER(ProfileRow), _I]),
     "sdg_forward_launches": (_I, [_P, _I, _I, _I]),
+    "sdg_profile_launches": (_I, [_P, _I, _I, _I, ctypes.c_char_p, _I, ctypes.POINTER(LaunchRow), _I]),
     "sdg_profile_category": (_I, [_P, _I, _I, _I, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
     "sdg_gemm_plan": (_I, [_I, _I, _I, _I, _I, _P]),
@@ -249,6 +255,15 @@ class Engine:
         check(lib().sdg_profile_category(self._h, B, H, W, categories.encode(), reps, ctypes.byref(ms),
                                          ctypes.byref(n), ctypes.byref(fl), ctypes.byref(by)))
         return ms.value, n.value, fl.value, by.value
+
+    def profile_launches(self, categories: str, B: int = 2, H: int = 64, W: int = 64, reps: int = 10) -> List[dict]:
+        """Per-launch device times of the forward's launches of the given categories, in forward order."""
+        rows = (LaunchRow * 1024)()
+        n = lib().sdg_profile_launches(self._h, B, H, W, categories.encode(), reps, rows, 1024)
+        if n < 0:
+            raise SdgError(-n, last_error())
+        return [{"label": rows[i].label.decode(), "category": rows[i].category.decode(), "ms": rows[i].ms,
+                 "flops": rows[i].flops, "bytes": rows[i].bytes} for i in range(n)]
 
     def forward_launches(self, B: int, H: int, W: int) -> int:
         return lib().sdg_forward_launches(self._h, B, H, W)

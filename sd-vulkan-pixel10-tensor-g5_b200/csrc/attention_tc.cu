@@ -397,11 +397,9 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         const int q0c = (h & 1) * 4;
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float x0 = ex2_approx(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new));
-          const float x1 = ex2_approx(fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new));
-          pk[e >> 1] = pack_half2(x0, x1);
-        }
+        for (int e = 0; e < 32; e += 2)  // exponent in fp16, 2^x two at a time (one MUFU op per pair)
+          pk[e >> 1] = ex2_f16x2(pack_half2(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new),
+                                            fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new)));
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
@@ -526,10 +524,16 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float x0 = ex2_approx(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new));
-          const float x1 = ex2_approx(fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new));
-          if constexpr (!ONES) rs += x0 + x1;
-          pk[e >> 1] = pack_half2(x0, x1);
+          if constexpr (ONES) {
+            // the ones row of V^T sums the fp16 P itself: exponent in fp16, 2^x two at a time
+            pk[e >> 1] = ex2_f16x2(pack_half2(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new),
+                                              fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new)));
+          } else {
+            const float x0 = ex2_approx(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new));
+            const float x1 = ex2_approx(fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new));
+            rs += x0 + x1;
+            pk[e >> 1] = pack_half2(x0, x1);
+          }
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {

@@ -130,8 +130,14 @@ class Builder {
   bool ctx_cached = false;
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof;
   // recording: every launch of the forward with its arguments, in issue order (replayed per
-  // category by sdg_profile_category to time one kind of kernel alone)
-  std::vector<std::pair<int, std::function<cudaError_t(cudaStream_t)>>>* rec = nullptr;
+  // category by sdg_profile_category, or one at a time by sdg_profile_launches)
+  struct Rec {
+    int cat;
+    std::string label;      // op and shape (GEMMs: the tile chooser's plan)
+    double flops, bytes;    // algorithmic work of this launch
+    std::function<cudaError_t(cudaStream_t)> fn;
+  };
+  std::vector<Rec>* rec = nullptr;
   double cat_flops[8] = {0}, cat_bytes[8] = {0};  // algorithmic work per category (counted in every mode)
 
  private:
@@ -199,9 +205,11 @@ class Builder {
   void begin_op(int cat);
   // One launch (nk kernels) of category `cat`: `f(stream)` issues it on s_, recorded when recording.
   template <typename F>
-  void issue(int cat, const char* what, int nk, F f) {
+  void issue(int cat, const char* what, int nk, F f, const std::string& label = std::string(), double fl = 0,
+             double by = 0) {
     begin_op(cat);
-    if (rec) rec->push_back({cat, std::function<cudaError_t(cudaStream_t)>(f)});
+    if (rec) rec->push_back({cat, label.empty() ? std::string(what) : label, fl, by,
+                             std::function<cudaError_t(cudaStream_t)>(f)});
     check(f(s_), what, cat, nk);
   }
   cudaEvent_t ev_start_ = nullptr;
@@ -586,7 +594,11 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
   if (dry_ || !ok()) { launches_ += groupnorm_launch_count(a); return; }
-  issue(kCatGN, "groupnorm", groupnorm_launch_count(a), [a](cudaStream_t s) { return launch_groupnorm(a, s); });
+  char lb[96];
+  snprintf(lb, sizeof lb, "groupnorm B=%d HW=%d C=%d%s%s", B, HW, a.C0 + a.C1, a.C1 ? " (concat)" : "",
+           silu ? " +silu" : "");
+  issue(kCatGN, "groupnorm", groupnorm_launch_count(a), [a](cudaStream_t s) { return launch_groupnorm(a, s); }, lb,
+        0.0, 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0)));
 }
 
 void Builder::gemm(GemmArgs a, int cat) {
@@ -599,8 +611,17 @@ void Builder::gemm(GemmArgs a, int cat) {
     off_ = mark;
     return;
   }
+  char lb[128];
+  if (rec) {
+    const GemmPlan pl = gemm_plan(a, a.ws_bytes > 0);
+    snprintf(lb, sizeof lb, "%s M=%d N=%d K=%d epi=%d | tile %dx%d%s ws-split %d cluster-split %d",
+             cat == kCatConv3 ? "conv3x3" : "gemm", a.M, a.N, a.K, a.epi, pl.pair ? 256 : 128, pl.bn,
+             pl.pair ? " pair" : "", pl.splits, pl.csplit);
+  } else {
+    lb[0] = 0;
+  }
   issue(cat, cat == kCatConv3 ? "conv3x3" : "gemm", gemm_launch_count(a),
-        [a, err = pl_.dev_err](cudaStream_t s) { return launch_gemm(a, err, s); });
+        [a, err = pl_.dev_err](cudaStream_t s) { return launch_gemm(a, err, s); }, lb, 2.0 * a.M * a.N * a.K);
   off_ = mark;
 }
 
@@ -704,7 +725,7 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
     if (dry_ || !ok()) { launches_++; return; }
     issue(kCatLN, "layernorm", 1, [=, g = n.g, b = n.b](cudaStream_t s) {
       return launch_layernorm(xin, M, C, g, b, kLnEps, hn, s);
-    });
+    }, "layernorm M=" + std::to_string(M) + " C=" + std::to_string(C), 0.0, 2.0 * 2.0 * M * C);
   };
   auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
                    int vt_idx, int spad) {
@@ -722,7 +743,10 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
     AttnArgs a;
     a.q = q; a.k = k; a.v = vt; a.BH = B * kHeads; a.heads = kHeads; a.Sq = S; a.Sk = Sk; a.d = d; a.dp = dp;
     a.d16 = d16; a.vt_ld = vt_ld; a.o = o; a.ld_o = C; a.scale = 1.0f / sqrtf((float)d);
-    issue(kCatAttn, "attention", 1, [a, err = pl_.dev_err](cudaStream_t s) { return launch_attention(a, err, s); });
+    issue(kCatAttn, "attention", 1, [a, err = pl_.dev_err](cudaStream_t s) { return launch_attention(a, err, s); },
+          "attention BH=" + std::to_string(a.BH) + " Sq=" + std::to_string(S) + " Sk=" + std::to_string(Sk) +
+              " d=" + std::to_string(d),
+          4.0 * B * kHeads * (double)S * Sk * d);
   };
   lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
   ln(tt, t.ln1);
@@ -1375,60 +1399,56 @@ SDG_API int sdg_profile(sdg_engine* h, int B, int H, int W, sdg_profile_row* row
   return n;
 }
 
-SDG_API int sdg_profile_category(sdg_engine* h, int B, int H, int W, const char* categories, int reps, double* ms,
-                                 int* launches, double* flops, double* bytes) {
-  if (!h) return SDG_ERR_NOT_INIT;
-  if (!categories || reps <= 0 || !ms) return fail(SDG_ERR_ARG, "profile_category: bad arguments");
-  bool want[sdg::kCatCount] = {false};
-  {
-    std::string list(categories);
-    size_t pos = 0;
-    while (pos <= list.size()) {
-      size_t end = list.find_first_of(",+", pos);
-      if (end == std::string::npos) end = list.size();
-      const std::string name = list.substr(pos, end - pos);
-      int c = 0;
-      while (c < sdg::kCatCount && name != sdg::kCatName[c]) ++c;
-      if (c == sdg::kCatCount) return fail(SDG_ERR_ARG, "profile_category: unknown category '" + name + "'");
-      want[c] = true;
-      pos = end + 1;
+extern "C++" {
+
+// Category names ("GN", "CONV3", ... joined by ',' or '+') -> mask; false on an unknown name.
+static bool parse_categories(const char* categories, bool (&want)[sdg::kCatCount]) {
+  for (bool& w : want) w = false;
+  std::string list(categories);
+  size_t pos = 0;
+  while (pos <= list.size()) {
+    size_t end = list.find_first_of(",+", pos);
+    if (end == std::string::npos) end = list.size();
+    const std::string name = list.substr(pos, end - pos);
+    int c = 0;
+    while (c < sdg::kCatCount && name != sdg::kCatName[c]) ++c;
+    if (c == sdg::kCatCount) {
+      fail(SDG_ERR_ARG, "unknown op category '" + name + "'");
+      return false;
     }
+    want[c] = true;
+    pos = end + 1;
   }
-  Engine& e = h->e;
-  cudaSetDevice(e.device);
-  sdg::Plan* p = nullptr;
-  int st = e.get_plan(B, H, W, 0, &p);
-  if (st) return st;
-  // 1) record the forward's launches with their arguments (captured, never launched)
-  std::vector<std::pair<int, std::function<cudaError_t(cudaStream_t)>>> rec;
+  return true;
+}
+
+// The forward's launches at plan p with their arguments, in issue order (captured, never launched).
+static int record_forward(Engine& e, sdg::Plan* p, std::vector<sdg::Builder::Rec>& rec) {
   sdg::Builder b(e, *p, false, e.stream);
   b.rec = &rec;
   if (cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-    return fail(SDG_ERR_CUDA, "profile_category: capture");
-  st = b.run();
+    return fail(SDG_ERR_CUDA, "profile: capture");
+  const int st = b.run();
   cudaGraph_t g0 = nullptr;
-  const cudaError_t ce0 = cudaStreamEndCapture(e.stream, &g0);
+  const cudaError_t ce = cudaStreamEndCapture(e.stream, &g0);
   if (g0) cudaGraphDestroy(g0);
   if (st != SDG_OK) return st;
-  if (ce0 != cudaSuccess) return fail(SDG_ERR_CUDA, std::string("profile_category: ") + cudaGetErrorString(ce0));
-  // 2) the selected launches alone, in forward order on one stream, as one graph
-  int n = 0;
+  if (ce != cudaSuccess) return fail(SDG_ERR_CUDA, std::string("profile: ") + cudaGetErrorString(ce));
+  return SDG_OK;
+}
+
+// Captures `issue(stream)` as one graph, replays it once to warm up and `reps` times between two events.
+template <typename F>
+static int time_graph(Engine& e, int reps, F issue, double* ms_per_rep) {
   if (cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
-    return fail(SDG_ERR_CUDA, "profile_category: capture");
-  cudaError_t le = cudaSuccess;
-  for (auto& r : rec)
-    if (want[r.first]) {
-      const cudaError_t x = r.second(e.stream);
-      if (x != cudaSuccess && le == cudaSuccess) le = x;
-      ++n;
-    }
+    return fail(SDG_ERR_CUDA, "profile: capture");
+  const cudaError_t le = issue(e.stream);
   cudaGraph_t g = nullptr;
   cudaGraphExec_t gx = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(e.stream, &g);
   cudaEvent_t e0 = nullptr, e1 = nullptr;
-  bool ok = le == cudaSuccess && ce == cudaSuccess && n > 0 && cudaGraphInstantiate(&gx, g, 0) == cudaSuccess &&
+  bool ok = le == cudaSuccess && ce == cudaSuccess && cudaGraphInstantiate(&gx, g, 0) == cudaSuccess &&
             cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
-  // 3) one warm-up replay, then `reps` replays back to back between two events
   ok = ok && cudaGraphLaunch(gx, e.stream) == cudaSuccess && cudaEventRecord(e0, e.stream) == cudaSuccess;
   for (int i = 0; ok && i < reps; ++i) ok = cudaGraphLaunch(gx, e.stream) == cudaSuccess;
   ok = ok && cudaEventRecord(e1, e.stream) == cudaSuccess;
@@ -1441,19 +1461,84 @@ SDG_API int sdg_profile_category(sdg_engine* h, int B, int H, int W, const char*
   if (g) cudaGraphDestroy(g);
   if (!ok) {
     cudaGetLastError();
-    return fail(n == 0 ? SDG_ERR_ARG : SDG_ERR_CUDA, n == 0 ? "profile_category: no launch of that category"
-                                                             : "profile_category: replay failed");
+    return fail(SDG_ERR_CUDA, "profile: replay failed");
   }
-  const int dev_status = e.check_dev_err(p, e.stream);
-  if (dev_status) return dev_status;
-  *ms = (double)t / reps;
+  *ms_per_rep = (double)t / reps;
+  return SDG_OK;
+}
+
+}  // extern "C++"
+
+SDG_API int sdg_profile_category(sdg_engine* h, int B, int H, int W, const char* categories, int reps, double* ms,
+                                 int* launches, double* flops, double* bytes) {
+  if (!h) return SDG_ERR_NOT_INIT;
+  if (!categories || reps <= 0 || !ms) return fail(SDG_ERR_ARG, "profile_category: bad arguments");
+  bool want[sdg::kCatCount];
+  if (!parse_categories(categories, want)) return SDG_ERR_ARG;
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return st;
+  std::vector<sdg::Builder::Rec> rec;
+  if ((st = record_forward(e, p, rec))) return st;
+  int n = 0;
   double fl = 0, by = 0;
-  for (int c = 0; c < sdg::kCatCount; ++c)
-    if (want[c]) { fl += b.cat_flops[c]; by += b.cat_bytes[c]; }
+  for (auto& r : rec)
+    if (want[r.cat]) { ++n; fl += r.flops; by += r.bytes; }
+  if (n == 0) return fail(SDG_ERR_ARG, "profile_category: no launch of that category");
+  // the selected launches alone, in forward order on one stream, as one graph
+  st = time_graph(e, reps, [&](cudaStream_t s) {
+    cudaError_t le = cudaSuccess;
+    for (auto& r : rec)
+      if (want[r.cat]) {
+        const cudaError_t x = r.fn(s);
+        if (x != cudaSuccess && le == cudaSuccess) le = x;
+      }
+    return le;
+  }, ms);
+  if (st) return st;
+  if ((st = e.check_dev_err(p, e.stream))) return st;
   if (launches) *launches = n;
   if (flops) *flops = fl;
   if (bytes) *bytes = by;
   return SDG_OK;
+}
+
+SDG_API int sdg_profile_launches(sdg_engine* h, int B, int H, int W, const char* categories, int reps,
+                                 sdg_launch_row* rows, int cap) {
+  if (!h) return -SDG_ERR_NOT_INIT;
+  if (!categories || reps <= 0 || !rows || cap <= 0) return -fail(SDG_ERR_ARG, "profile_launches: bad arguments");
+  bool want[sdg::kCatCount];
+  if (!parse_categories(categories, want)) return -SDG_ERR_ARG;
+  Engine& e = h->e;
+  cudaSetDevice(e.device);
+  sdg::Plan* p = nullptr;
+  int st = e.get_plan(B, H, W, 0, &p);
+  if (st) return -st;
+  std::vector<sdg::Builder::Rec> rec;
+  if ((st = record_forward(e, p, rec))) return -st;
+  int n = 0;
+  for (auto& r : rec) {
+    if (!want[r.cat]) continue;
+    if (n >= cap) break;
+    double ms = 0;
+    // `reps` copies of this one launch back to back in a graph, replayed once
+    st = time_graph(e, 1, [&](cudaStream_t s) {
+      cudaError_t le = cudaSuccess;
+      for (int i = 0; i < reps && le == cudaSuccess; ++i) le = r.fn(s);
+      return le;
+    }, &ms);
+    if (st) return -st;
+    sdg_launch_row& row = rows[n++];
+    snprintf(row.label, sizeof row.label, "%s", r.label.c_str());
+    snprintf(row.category, sizeof row.category, "%s", sdg::kCatName[r.cat]);
+    row.ms = ms / reps;
+    row.flops = r.flops;
+    row.bytes = r.bytes;
+  }
+  if ((st = e.check_dev_err(p, e.stream))) return -st;
+  return n;
 }
 
 }  // extern "C"

@@ -53,6 +53,18 @@ def build_ops(sdg, dev):
         ya = torch.empty((M, N), dtype=torch.float16, device=dev)
         ops[f"linear_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ya=ya: sdg.linear(xa, wa, out=ya), 2.0 * M * N * K, 0.0)
         ops[f"cublas_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ya=ya: torch.matmul(xa, wa.t(), out=ya), 2.0 * M * N * K, 0.0)
+    # the forward's most frequent linear shapes: K=320 out-projection with residual, the GEGLU FF-proj,
+    # and the 32x32 / 16x16-level projections
+    for M, N, K, act, res in ((8192, 320, 320, 0, True), (8192, 2560, 320, 2, False), (2048, 640, 640, 0, True),
+                              (512, 1280, 1280, 0, True), (8192, 320, 1280, 0, True)):
+        xa = rn(M, K)
+        wa = rn(N, K, std=0.02)
+        ba = torch.zeros(N, device=dev)
+        ra = rn(M, N) if res else None
+        ya = torch.empty((M, N // 2 if act == 2 else N), dtype=torch.float16, device=dev)
+        tag = "geglu" if act == 2 else ("linres" if res else "lin")
+        ops[f"{tag}_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ba=ba, ra=ra, ya=ya, act=act:
+                                     sdg.linear(xa, wa, ba, residual=ra, act=act, out=ya), 2.0 * M * N * K, 0.0)
     x = rn(B, 32, 32, 320)                                                  # config 1 conv1x1 skip
     w = rn(640, 320, std=0.02)
     y = torch.empty((B, 32, 32, 640), dtype=torch.float16, device=dev)
