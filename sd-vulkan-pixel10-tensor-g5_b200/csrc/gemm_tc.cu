@@ -205,6 +205,19 @@ struct EpiIn {
   uint4 res[CH / 8];  // residual (fp16)
 };
 
+// Residual of one CH-column chunk of row m (zero where absent): issued a chunk ahead of its use,
+// and for a tile's first chunk before the accumulator wait, so its L2 latency overlaps the main
+// loop or the previous chunk instead of adding to each chunk.
+template <int CH>
+__device__ __forceinline__ void res_load(const GemmDev& p, int m, int n, bool mvalid, uint4 (&res)[CH / 8]) {
+#pragma unroll
+  for (int g = 0; g < CH / 8; ++g)
+    res[g] = (mvalid && p.residual && n + 8 * g < p.N)
+                 ? __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.ld_res + n) + g)
+                 : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Bias and per-image row bias of one chunk (the residual comes from res_load).
 template <int CH>
 __device__ __forceinline__ void epi_load(const GemmDev& p, int m, int img, int n, bool mvalid, EpiIn<CH>& in) {
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -221,11 +234,8 @@ __device__ __forceinline__ void epi_load(const GemmDev& p, int m, int img, int n
       in.b[q].x += t.x; in.b[q].y += t.y; in.b[q].z += t.z; in.b[q].w += t.w;
     }
   }
-#pragma unroll
-  for (int g = 0; g < CH / 8; ++g)
-    in.res[g] = (mvalid && p.residual && n + 8 * g < p.N)
-                    ? __ldg(reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.ld_res + n) + g)
-                    : make_uint4(0u, 0u, 0u, 0u);
+  (void)m;
+  (void)mvalid;
 }
 
 // Fused epilogue of one chunk (plain or attention-head outputs) from the accumulator words r and
@@ -564,6 +574,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       const int n0 = n_blk * BN;
       const bool mvalid = m < p.M;
       if (p.splits == 1 && csp == 1 && p.epi != kEpiGeglu) epi_prefetch<C::kChunk>(p, m, img, n0 + eh * C::kChunk, mvalid);
+      // the first chunk's residual, in flight while the main loop finishes
+      uint4 res_next[C::kChunk / 8];
+      const bool fused_res = csp == 1 && p.splits == 1 && p.epi != kEpiNchwF32 && p.epi != kEpiGeglu && p.residual;
+      if (fused_res) res_load<C::kChunk>(p, m, n0 + eh * C::kChunk, mvalid, res_next);
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc, p.wait_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -623,7 +637,8 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
                   gt *= __ldg(p.wscale + n0 + HALF + cj);
                 }
                 a += bav[j];
-                gt += bgv[j];                v[j] = a * gelu_erf(gt);
+                gt += bgv[j];
+                v[j] = a * gelu_as(gt);
               }
               *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc + g * 8) = pack8(v);
 #pragma unroll
@@ -648,6 +663,11 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           const bool fused = p.splits == 1 && p.epi != kEpiNchwF32;
           EpiIn<CH> in;
           if (fused) epi_load<CH>(p, m, img, n, mvalid, in);  // in flight with the TMEM load
+          if (fused_res) {
+#pragma unroll
+            for (int g = 0; g < CH / 8; ++g) in.res[g] = res_next[g];
+            if (c + kSplit * CH < BN) res_load<CH>(p, m, n + kSplit * CH, mvalid, res_next);  // next chunk's
+          }
           tmem_wait_ld();
           if (!mvalid || n >= p.N) continue;
           if (fused) {

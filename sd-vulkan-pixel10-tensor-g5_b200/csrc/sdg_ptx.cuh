@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevTimeoutAcc = 0x103,    // MMA/epilogue waited too long on an accumulator
   kDevTimeoutAttn = 0x104,   // attention pipeline wait expired
   kDevTimeoutDrain = 0x105,  // drain of in-flight copies on an abort path
+  kDevTimeoutGrid = 0x106,   // grid-wide barrier (GroupNorm) waited too long for the other CTAs
   kDevBadShape = 0x201,      // a kernel's own shape guard rejected its arguments
 };
 
@@ -350,6 +351,28 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
   return y;
 }
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Exact-erf GELU, x * Phi(x), with erf from Abramowitz & Stegun, Handbook of Mathematical
+// Functions, formula 7.1.26 (Hastings' approximation; absolute error <= 1.5e-7 for z >= 0):
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z).
+// With z = |x| / sqrt(2) and q = (a1 t + ... + a5 t^5) exp(-z^2): Phi(x) = 1 - q/2 for x >= 0
+// and q/2 for x < 0 (no cancellation on the negative side). Two MUFU operations (reciprocal,
+// exp2) and ~10 FMA-pipe operations.
+__device__ __forceinline__ float gelu_as(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float hq = 0.5f * poly * ex2_approx(-1.4426950408889634f * z * z);
+  return x * (x >= 0.f ? 1.0f - hq : hq);
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);

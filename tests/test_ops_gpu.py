@@ -70,6 +70,27 @@ def test_linear_geglu(sdg, cuda, gen):
     assert rel(y, ref) < TOL
 
 
+def test_geglu_gelu_accuracy(sdg, cuda):
+    """The GEGLU epilogue's GELU (erf from Abramowitz & Stegun 7.1.26) against exact erf GELU in
+    fp64: value input 1 and gate input u swept over [-8, 8], so each output is fp16(gelu(u))."""
+    M, K = 4096, 64
+    u = torch.linspace(-8.0, 8.0, M).half()
+    x = torch.zeros(M, K, dtype=torch.float16)
+    x[:, 0] = u
+    x[:, 1] = 1.0
+    w = torch.zeros(256, K, dtype=torch.float16)   # rows 0..127 value, 128..255 gate
+    w[:128, 1] = 1.0
+    w[128:, 0] = 1.0
+    wp, _ = sdg.pack_geglu_weight(w.to(cuda))
+    y = sdg.linear(x.to(cuda), wp, torch.zeros(256, device=cuda), act=2)
+    torch.cuda.synchronize()
+    ref = F.gelu(u.double())
+    got = y.double().cpu()
+    assert torch.equal(got, got[:, :1].expand_as(got))        # every column holds the same value
+    err = (got[:, 0] - ref).abs()
+    assert bool((err <= ref.abs() * 2.0 ** -11 + 2e-6).all()), float(err.max())
+
+
 # ---------------------------------------------------------------- conv
 def nhwc(x):
     return x.permute(0, 2, 3, 1).contiguous()
@@ -143,6 +164,8 @@ def test_conv3x3_stride2(sdg, cuda, gen, C, H):
 @pytest.mark.parametrize("B,C,H,silu,eps,shift", [
     (2, 320, 64, True, 1e-5, 0.0), (2, 1280, 16, True, 1e-5, 0.0),                   # config 1
     (2, 640, 32, False, 1e-6, 3.0), (1, 2560, 8, True, 1e-5, -2.0), (2, 960, 64, True, 1e-5, 0.5),
+    (8, 960, 32, True, 1e-5, 0.0),    # single launch with a grid-wide barrier (up to one CTA per SM)
+    (16, 320, 64, True, 1e-5, 1.0),   # too large for one CTA per SM: the cluster kernel
 ])
 def test_groupnorm(sdg, cuda, gen, B, C, H, silu, eps, shift):
     x = (rnd(B, C, H, H, g=gen) * 1.5 + shift).half()
