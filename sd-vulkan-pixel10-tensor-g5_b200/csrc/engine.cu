@@ -108,7 +108,6 @@ struct Plan {
   float* lat_in = nullptr; float* t_in = nullptr; float* tproj_in = nullptr; float* ctx_in = nullptr;
   float* out = nullptr;
   int* dev_err = nullptr;
-  unsigned* gn_sync = nullptr;  // GroupNorm grid-barrier words (zero between launches)
   int launches = 0;
 };
 
@@ -592,8 +591,6 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
   a.B = B; a.HW = HW; a.groups = 32;
   a.gamma = n.g; a.beta = n.b; a.eps = eps; a.silu = silu ? 1 : 0; a.y = y;
   a.stats = static_cast<float*>(alloc(groupnorm_scratch_bytes(B, HW, a.C0 + a.C1, 32)));  // scope scratch
-  a.sync = pl_.gn_sync;
-  a.err = pl_.dev_err;
   gn_slot_++;
   cat_bytes[kCatGN] += 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0));
   if (dry_ || !ok()) { launches_ += groupnorm_launch_count(a); return; }
@@ -830,7 +827,6 @@ int Builder::run() {
   pl_.ctx_in = alloc_f((size_t)B * kCtxLen * kCtxDim);
   pl_.out = alloc_f((size_t)B * 4 * HW);
   pl_.dev_err = static_cast<int*>(alloc(256));
-  pl_.gn_sync = static_cast<unsigned*>(alloc(256));
   {
     int h = H, ww = W;
     for (int i = 0; i < 3; ++i) { level_bufs(kBlockOut[i], h * ww); h /= 2; ww /= 2; }
@@ -1054,7 +1050,6 @@ int Engine::check_dev_err(Plan* p, cudaStream_t s) {
   SDG_CUDA_TRY(cudaStreamSynchronize(s));
   if (v != 0) {
     cudaMemsetAsync(p->dev_err, 0, 4, s);
-    cudaMemsetAsync(p->gn_sync, 0, 8, s);  // a barrier that timed out leaves its count behind
     cudaStreamSynchronize(s);
     char buf[96];
     snprintf(buf, sizeof buf, "device error word 0x%x (a kernel's bounded wait expired)", v);

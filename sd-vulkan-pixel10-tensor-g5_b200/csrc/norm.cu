@@ -386,256 +386,6 @@ int gn_fused_cluster(int C, int groups, int HW, int ns) {
   return gn_cluster_ctas(HW, C / ns, kGnMaxCluster);
 }
 
-// Single-launch GroupNorm without clusters: B * K CTAs of 512 threads (at most one per SM, so
-// all are resident together), K per image, each owning a contiguous range of the image's pixels
-// over all its channels. Every thread issues all loads of its share up front (at most kGnGridMaxV
-// 16-byte vectors in registers). Each CTA reduces its range exactly (mean, then centred sum of
-// squares, in a fixed order) and writes one (mean, M2) pair per group; after one grid-wide
-// barrier every CTA merges the K pairs of its image in order k = 0..K-1 with the pairwise update
-// of Chan, Golub and LeVeque (deterministic, independent of the rest of the batch), then
-// normalises from registers. The barrier is a sense-reversing counter: arrivals wrap back to
-// zero (atomicInc) and the last arrival advances a generation word the others wait on; the
-// wait is bounded (error word + early return, no normalisation, on expiry).
-constexpr int kGnGridThreads = 512;
-constexpr int kGnGridMaxV = 16;
-constexpr int kGnGridMaxGroups = 64;
-constexpr int kGnGridMaxPer = 8;  // (mean, M2) pairs each merging thread loads: K <= 8 * threads per group
-
-// Threads merging one group's pairs after the barrier: a power of two, at most a warp.
-__host__ __device__ __forceinline__ int gn_grid_tpg(int groups) {
-  int tpg = 32;
-  while (tpg > 1 && tpg * groups > kGnGridThreads) tpg >>= 1;
-  return tpg;
-}
-
-// Pairwise update of Chan, Golub and LeVeque: (n, m, m2) absorbs the aggregate (nb, mb, m2b).
-__device__ __forceinline__ void chan_merge(float& n, float& m, float& m2, float nb, float mb, float m2b) {
-  if (nb <= 0.f) return;
-  const float nn = n + nb;
-  const float d = mb - m;
-  m += d * (nb / nn);
-  m2 += m2b + d * d * (n * nb / nn);
-  n = nn;
-}
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Every CTA of the grid arrives; returns false (after recording kDevTimeoutGrid) if the others did
-// not all arrive within the wait limit. The CTA's global writes before the call are visible to
-// every CTA after it.
-__device__ __forceinline__ bool grid_barrier(unsigned* sync, unsigned nblocks, int* err) {
-  __threadfence();
-  __syncthreads();
-  int ok = 1;
-  if (threadIdx.x == 0) {
-    const unsigned gen = ld_acquire_u32(sync + 1);
-    const unsigned old = atomicInc(sync, nblocks - 1);  // the last arrival wraps the count to 0
-    if (old == nblocks - 1) {
-      __threadfence();
-      atomicAdd(sync + 1, 1u);
-    } else {
-      const uint64_t t0 = globaltimer();
-      for (unsigned i = 1; ld_acquire_u32(sync + 1) == gen; ++i) {
-        __nanosleep(64);
-        if ((i & 63u) == 0u && globaltimer() - t0 > kWaitTimeoutNs) {
-          if (err) atomicCAS(err, 0, kDevTimeoutGrid);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    __threadfence();
-  }
-  return __syncthreads_and(ok) != 0;
-}
-
-__global__ void __launch_bounds__(kGnGridThreads, 1)
-    gn_grid_kernel(GroupNormArgs a, int K, float2* __restrict__ gstat, float2* __restrict__ part, unsigned* sync) {
-  pdl_wait();
-  // Dependents launch only once every CTA of this grid has started (and so is resident): the
-  // grid barrier below cannot be starved by the next kernel's CTAs.
-  pdl_trigger();
-  const int k = blockIdx.x % K, img = blockIdx.x / K;
-  const int C = a.C0 + a.C1, G = a.groups, cpg = C / G;
-  const int nv = C / 8;
-  const int rows = kGnGridThreads / nv;
-  const int chunk = (a.HW + K - 1) / K;
-  const int p0 = min(a.HW, k * chunk), p1 = min(a.HW, p0 + chunk);
-  const int t = threadIdx.x, v = t % nv, r = t / nv;
-  const bool active = r < rows;
-  const int c0 = v * 8;
-  const int cnt = (active && p0 + r < p1) ? (p1 - p0 - r + rows - 1) / rows : 0;
-  const float n_loc = (float)(p1 - p0) * cpg;
-  const size_t img_base = (size_t)img * a.HW;
-  __shared__ float red[kGnGridThreads * 8];  // [rows][C] per-thread channel partials (rows * C <= 8 * threads)
-  __shared__ float chan[kGnMaxC];            // channel sums, then per-channel scale
-  __shared__ float shf[kGnMaxC];             // per-channel shift
-  __shared__ float gsum[kGnGridMaxGroups], gmu[kGnGridMaxGroups], grs[kGnGridMaxGroups];
-
-  uint4 xs[kGnGridMaxV];
-  int cl;
-  const __half* src0 = gn_src(a, c0, img_base + p0 + r, cl);
-  const size_t pstride = (size_t)rows * (c0 < a.C0 ? a.C0 : a.C1);
-#pragma unroll
-  for (int i = 0; i < kGnGridMaxV; ++i)
-    if (i < cnt) xs[i] = *reinterpret_cast<const uint4*>(src0 + cl + i * pstride);
-
-  auto unpack = [](const uint4& u, float (&x)[8]) {
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h[e]);
-      x[2 * e] = f.x;
-      x[2 * e + 1] = f.y;
-    }
-  };
-  // per-thread channel partials -> per-group CTA sums in gsum (fixed order)
-  auto group_sums = [&](const float (&acc)[8]) {
-    if (active) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) red[r * C + c0 + e] = acc[e];
-    }
-    __syncthreads();
-    for (int c = t; c < C; c += kGnGridThreads) {
-      float s = 0.f;
-      for (int rr = 0; rr < rows; ++rr) s += red[rr * C + c];
-      chan[c] = s;
-    }
-    __syncthreads();
-    for (int g = t >> 5; g < G; g += kGnGridThreads / 32) {
-      float s = 0.f;
-      for (int j = t & 31; j < cpg; j += 32) s += chan[g * cpg + j];
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if ((t & 31) == 0) gsum[g] = s;
-    }
-    __syncthreads();
-  };
-
-  float acc[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll
-  for (int i = 0; i < kGnGridMaxV; ++i) {
-    if (i < cnt) {
-      float x[8];
-      unpack(xs[i], x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += x[e];
-    }
-  }
-  group_sums(acc);
-  float mu[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    acc[e] = 0.f;
-    mu[e] = n_loc > 0.f ? gsum[(c0 + e) / cpg] / n_loc : 0.f;
-  }
-  float cmean = 0.f;
-  if (t < G) cmean = n_loc > 0.f ? gsum[t] / n_loc : 0.f;
-#pragma unroll
-  for (int i = 0; i < kGnGridMaxV; ++i) {
-    if (i < cnt) {
-      float x[8];
-      unpack(xs[i], x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float d = x[e] - mu[e];
-        acc[e] += d * d;
-      }
-    }
-  }
-  __syncthreads();  // every read of gsum (the means) is done before group_sums rewrites it
-  group_sums(acc);
-  if (t < G) part[((size_t)img * K + k) * G + t] = make_float2(cmean, gsum[t]);
-  if (!grid_barrier(sync, gridDim.x, a.err)) return;
-  {
-    // Merge the image's K pairs per group: tpg threads per group each load their pairs
-    // q = j, j + tpg, ... at once (one L2 round trip) and merge them in increasing q, then the
-    // tpg partial aggregates are combined by a fixed shuffle tree (deterministic).
-    const int tpg = gn_grid_tpg(G);
-    const int g = t / tpg, j = t % tpg;
-    float n = 0.f, m = 0.f, m2 = 0.f;
-    if (g < G) {
-      const float2* pp = part + (size_t)img * K * G + g;
-      float2 pb[kGnGridMaxPer];
-#pragma unroll
-      for (int u = 0; u < kGnGridMaxPer; ++u) {
-        const int q = j + u * tpg;
-        if (q < K) pb[u] = __ldcg(pp + (size_t)q * G);  // L2: other CTAs' writes
-      }
-#pragma unroll
-      for (int u = 0; u < kGnGridMaxPer; ++u) {
-        const int q = j + u * tpg;
-        if (q >= K) break;
-        const int qa = min(a.HW, q * chunk), qb = min(a.HW, qa + chunk);
-        chan_merge(n, m, m2, (float)(qb - qa) * cpg, pb[u].x, pb[u].y);
-      }
-    }
-    for (int off = tpg >> 1; off > 0; off >>= 1) {
-      const float nb = __shfl_down_sync(0xffffffffu, n, off, tpg);
-      const float mb = __shfl_down_sync(0xffffffffu, m, off, tpg);
-      const float m2b = __shfl_down_sync(0xffffffffu, m2, off, tpg);
-      chan_merge(n, m, m2, nb, mb, m2b);
-    }
-    if (g < G && j == 0) {
-      gmu[g] = m;
-      grs[g] = rsqrtf(m2 / n + a.eps);
-    }
-  }
-  __syncthreads();
-  if (k == 0 && t < G && gstat) gstat[img * G + t] = make_float2(gmu[t], grs[t]);
-  for (int c = t; c < C; c += kGnGridThreads) {
-    const int g = c / cpg;
-    const float sc = grs[g] * a.gamma[c];
-    chan[c] = sc;
-    shf[c] = a.beta[c] - gmu[g] * sc;
-  }
-  __syncthreads();
-  if (cnt > 0) {
-    float scl[8], sh8[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) { scl[e] = chan[c0 + e]; sh8[e] = shf[c0 + e]; }
-    __half* dst0 = a.y + (img_base + p0 + r) * C + c0;
-#pragma unroll
-    for (int i = 0; i < kGnGridMaxV; ++i) {
-      if (i < cnt) {
-        float x[8];
-        unpack(xs[i], x);
-        uint4 o;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float y0 = x[2 * e] * scl[2 * e] + sh8[2 * e];
-          float y1 = x[2 * e + 1] * scl[2 * e + 1] + sh8[2 * e + 1];
-          if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
-          ow[e] = pack_half2(y0, y1);
-        }
-        *reinterpret_cast<uint4*>(dst0 + (size_t)i * rows * C) = o;
-      }
-    }
-  }
-}
-
-// CTAs per image for gn_grid_kernel (0: the shape does not fit it). About 32 KB of input per
-// CTA, B * K <= the SM count, and each thread's share within kGnGridMaxV vectors.
-int gn_grid_ctas(int B, int HW, int C, int groups) {
-  if (groups > kGnGridMaxGroups || C % 8 || C > kGnMaxC) return 0;
-  const int nv = C / 8;
-  if (nv > kGnGridThreads) return 0;
-  const int rows = kGnGridThreads / nv;
-  const int kmax = num_sms() / B;
-  if (kmax < 1) return 0;
-  const long bytes = (long)HW * C * 2;
-  const int kcap = std::min(kmax, kGnGridMaxPer * gn_grid_tpg(groups));
-  int K = (int)std::min<long>(kcap, std::max<long>(1, (bytes + 32767) / 32768));
-  while (K <= kcap && ((HW + K - 1) / K + rows - 1) / rows > kGnGridMaxV) ++K;
-  return K <= kcap ? K : 0;
-}
-
 // LayerNorm over C per token: one warp per token, values kept in registers,
 // exact centred variance. Replaces layernorm_f32.comp (vk_engine.cpp:652).
 template <int VPL>  // 8-channel vectors per lane
@@ -710,16 +460,13 @@ __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, i
 // Pixels per apply block: ~32 KB of input, depends only on (HW, C).
 static int gn_ppb(int HW, int C) { return std::max(1, std::min(HW, (32 * 1024) / (2 * C))); }
 
-// Scratch: (mean, rstd) per (image, group) first; for gn_grid_kernel then one (mean, M2) pair per
-// (CTA, group) and the barrier's two words.
 size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups) {
-  const size_t base = (size_t)B * groups * sizeof(float2);
-  const int K = gn_grid_ctas(B, HW, C, groups);
-  return K ? base + (size_t)B * K * groups * sizeof(float2) + 16 : base;
+  (void)HW;
+  (void)C;
+  return (size_t)B * groups * sizeof(float2);
 }
 
 int groupnorm_launch_count(const GroupNormArgs& a) {
-  if (gn_grid_ctas(a.B, a.HW, a.C0 + a.C1, a.groups)) return 1;
   return (a.groups <= 32 && gn_fused_slices(a.C0 + a.C1, a.groups, a.HW) > 0) ? 1 : 2;
 }
 
@@ -729,17 +476,6 @@ cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s) {
       C % a.groups || (C / a.groups) % 2 || a.HW <= 0 || a.B <= 0 || !a.stats || !a.y || !a.gamma || !a.beta)
     return cudaErrorInvalidValue;
   float2* gstat = reinterpret_cast<float2*>(a.stats);
-  const int K = gn_grid_ctas(a.B, a.HW, C, a.groups);
-  if (K > 0) {
-    float2* part = gstat + (size_t)a.B * a.groups;
-    unsigned* sync = a.sync;
-    if (!sync) {  // barrier words at the end of the scratch, cleared for this call
-      sync = reinterpret_cast<unsigned*>(part + (size_t)a.B * K * a.groups);
-      const cudaError_t e = cudaMemsetAsync(sync, 0, 2 * sizeof(unsigned), s);
-      if (e != cudaSuccess) return e;
-    }
-    return launch_kernel(gn_grid_kernel, dim3(a.B * K), dim3(kGnGridThreads), 0, s, 0, a, K, gstat, part, sync);
-  }
   const int ns = a.groups <= 32 ? gn_fused_slices(C, a.groups, a.HW) : 0;
   static bool cluster_ok[64] = {false};
   int dev = 0;

@@ -70,11 +70,8 @@ struct GemmPlan {
 GemmPlan gemm_plan(const GemmArgs& a, bool with_workspace);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
-// tensors. stats: groupnorm_scratch_bytes() bytes, any contents; receives
-// (mean, rstd) per (image, group) as float2 [B][groups] at its start.
-// sync (optional): two words for the single-launch kernel's grid-wide barrier,
-// zero on entry and left zero by every launch that completes; when null the
-// launch takes them from the end of stats and clears them first (a memset).
+// tensors. stats: groupnorm_scratch_bytes() bytes; receives (mean, rstd) per
+// (image, group) as float2 [B][groups].
 struct GroupNormArgs {
   const __half* x0 = nullptr; const __half* x1 = nullptr;
   int C0 = 0, C1 = 0, B = 1, HW = 1, groups = 32;
@@ -82,8 +79,6 @@ struct GroupNormArgs {
   float eps = 1e-5f; int silu = 1;
   __half* y = nullptr;
   float* stats = nullptr;
-  unsigned* sync = nullptr;
-  int* err = nullptr;  // device error word for the barrier's bounded wait (may be null)
 };
 cudaError_t launch_groupnorm(const GroupNormArgs& a, cudaStream_t s);
 size_t groupnorm_scratch_bytes(int B, int HW, int C, int groups);

@@ -22,7 +22,6 @@ enum DeviceError : int {
   kDevTimeoutAcc = 0x103,    // MMA/epilogue waited too long on an accumulator
   kDevTimeoutAttn = 0x104,   // attention pipeline wait expired
   kDevTimeoutDrain = 0x105,  // drain of in-flight copies on an abort path
-  kDevTimeoutGrid = 0x106,   // grid-wide barrier (GroupNorm) waited too long for the other CTAs
   kDevBadShape = 0x201,      // a kernel's own shape guard rejected its arguments
 };
 
