@@ -233,12 +233,19 @@ def run_config3(eng, sdg, dev, world, rank, sizes=(8, 16, 64), steps=4, cfg=1.5)
         got = mg.lcm_generate(eng.lcm_denoise, lat, cond, unc, noise, steps=steps, cfg=cfg, device=dev, timings=tm)
         tot = time.perf_counter() - t0
         v = torch.tensor([tot, tm["denoise_s"], tm["gather_s"]], dtype=torch.float64, device=dev)
+        vmin = v.clone()
         if world > 1:
             dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            dist.all_reduce(vmin, op=dist.ReduceOp.MIN)
         tot, den, gat = (float(x) for x in v.tolist())
+        den_min, gat_min = float(vmin[1]), float(vmin[2])
+        # a rank's gather time = waiting for the slowest rank's denoise + the transfer itself: the
+        # fastest rank's wait minus the spread of the denoise times bounds the transfer
         rec = {"images": n, "images_per_gpu": mg.shard(n, world, 0)[1], "s": tot, "images_per_s": n / tot,
-               "unet_fwd_per_s": n * steps / tot, "denoise_s_max": den, "gather_s_max": gat,
-               "gather_share": gat / tot}
+               "unet_fwd_per_s": n * steps / tot, "denoise_s_max": den, "denoise_s_min": den_min,
+               "gather_s_max": gat, "gather_s_min": gat_min, "gather_share": gat / tot,
+               "limiter": ("straggler (denoise spread across ranks)" if world > 1 and den - den_min > gat_min
+                           else ("gather" if world > 1 else "none (1 rank)"))}
         if rank == 0:
             ref = []
             for r in range(world):          # each rank's shard, recomputed here with the same chunking
