@@ -490,7 +490,9 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           const int nsub = min(G, kb1 - kb);
           if (!mbar_wait(full_bar(s), ph, p.err, kDevTimeoutFull, p.wait_ns)) { ok = false; break; }
           if (W8 && !mbar_wait(conv_bar(s), ph, p.err, kDevTimeoutFull, p.wait_ns)) { ok = false; break; }
-          tc_fence_after();
+          // No tcgen05 fence here: the stage's operands are shared memory written by TMA (or by the
+          // converter warps, fenced to the async proxy before their arrive), ordered by the mbarrier
+          // itself; the accumulator (TMEM) hazard was fenced once per tile after the tempty wait.
 #pragma unroll
           for (int g = 0; g < G; ++g) {
             if (g >= nsub) break;
