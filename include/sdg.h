@@ -217,8 +217,8 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
                        size_t workspace_bytes, int* err_word, void* stream);
 
 /* y[M,N] = x[M,K] * w[N,K]^T (+bias) (+residual) (act: 0 none, 1 SiLU,
- * 2 GEGLU: w rows arranged in 256-row tiles [128 value rows ; 128 gate rows],
- * y is [M, N/2]). */
+ * 2 GEGLU: w rows interleaved in groups of 16, [16 value rows ; the matching 16 gate
+ * rows] repeated (bias likewise), y is [M, N/2]; N a multiple of 64). */
 SDG_API int sdg_linear(const uint16_t* x, int M, int K, const uint16_t* w, const float* bias, int N,
                        const uint16_t* residual, int act, uint16_t* y, void* workspace, size_t workspace_bytes,
                        int* err_word, void* stream);

@@ -307,7 +307,7 @@ def gemm_plan(M: int, N: int, K: int, taps: int = 1, workspace: bool = True) -> 
 
 
 def linear(x, w, bias=None, residual=None, act: int = 0, out=None, workspace=None, err_word=None, stream=None):
-    """x [M,K] fp16, w [N,K] fp16 -> [M,N] (act 2 = GEGLU on 256-row [value;gate] tiles -> [M,N/2])."""
+    """x [M,K] fp16, w [N,K] fp16 -> [M,N] (act 2 = GEGLU, w packed by pack_geglu_weight -> [M,N/2])."""
     import torch
     M, K = x.shape
     N = w.shape[0]
@@ -427,15 +427,16 @@ def pack_conv_weight(w_torch):
     return w_torch.permute(0, 2, 3, 1).reshape(Co, kh * kw * Ci).contiguous()
 
 
-def pack_geglu_weight(w_torch, b_torch=None, tile: int = 256):
-    """FF-proj [8C, C] (rows: value half then gate half) -> 256-row tiles [128 value ; 128 gate]."""
+def pack_geglu_weight(w_torch, b_torch=None, group: int = 16):
+    """FF-proj [8C, C] (rows: value half then gate half) -> rows interleaved in groups of 16:
+    [16 value rows ; the matching 16 gate rows] repeated (the layout the GEGLU epilogue reads)."""
     import torch
     N = w_torch.shape[0]
     half = N // 2
     idx = []
-    for t in range(N // tile):
-        idx += list(range(t * (tile // 2), (t + 1) * (tile // 2)))
-        idx += list(range(half + t * (tile // 2), half + (t + 1) * (tile // 2)))
+    for t in range(half // group):
+        idx += list(range(t * group, (t + 1) * group))
+        idx += list(range(half + t * group, half + (t + 1) * group))
     idx_t = torch.tensor(idx, device=w_torch.device)
     wp = w_torch.index_select(0, idx_t).contiguous()
     bp = None if b_torch is None else b_torch.index_select(0, idx_t).contiguous()

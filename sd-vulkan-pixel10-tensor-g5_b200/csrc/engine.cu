@@ -499,7 +499,7 @@ int Engine::prepare() {
       P.linear_rows(o, C, kCtxDim, b + ".attn2.to_v.weight", kCtxDim, C);
     }
     P.linear(t.out2, b + ".attn2.to_out.0", C, C, true);
-    {  // GEGLU proj [8C][C] re-tiled: each 256-row tile = [128 value rows ; 128 gate rows]
+    {  // GEGLU proj [8C][C] interleaved: rows 32j..32j+15 = value rows 16j.., 32j+16..32j+31 = gate rows 16j..
       const int N = 8 * C, half = 4 * C;
       t.ff1.N = N; t.ff1.K = C;
       size_t tmp = P.reserve((size_t)N * C * 2);  // unreordered copy (host staging only)
@@ -514,8 +514,8 @@ int Engine::prepare() {
       uint16_t* dst = reinterpret_cast<uint16_t*>(P.staging.data() + o);
       float* bd = reinterpret_cast<float*>(P.staging.data() + bo);
       for (int r = 0; r < N; ++r) {
-        const int tile = r / 256, within = r % 256;
-        const int srow = within < 128 ? tile * 128 + within : half + tile * 128 + (within - 128);
+        const int grp = r / 32, within = r % 32;
+        const int srow = within < 16 ? grp * 16 + within : half + grp * 16 + (within - 16);
         memcpy(dst + (size_t)r * C, src + (size_t)srow * C, (size_t)C * 2);
         bd[r] = hb ? h2f(hb->data[srow]) : 0.f;
       }

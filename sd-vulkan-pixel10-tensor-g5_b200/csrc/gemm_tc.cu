@@ -653,68 +653,45 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         // cluster K split: the partial tile stays in TMEM until every CTA of the cluster is
         // past its main loop (reduction below)
       } else if (p.epi == kEpiGeglu) {
-        constexpr int HALF = BN / 2;
-        const int nout0 = n_blk * HALF;
+        // GEGLU: W rows interleave 16 value rows and 16 gate rows, so each 32-column chunk of the
+        // accumulator holds 16 value columns then their 16 gate columns, and yields 16 outputs
+        // (output column = packed column / 2) -- any tile width that is a multiple of 32 works.
+        if constexpr (CH == 32) {  // (tiles narrower than 32 columns never take GEGLU)
 #pragma unroll 1
-        for (int c = eh * CH; c < HALF; c += kSplit * CH) {
-          if (p.bias && c + kSplit * CH < HALF) {
-            prefetch_l1(p.bias + n0 + c + kSplit * CH);
-            prefetch_l1(p.bias + n0 + HALF + c + kSplit * CH);
-          }
-          uint32_t ra[32], rg[32];
-          if constexpr (CH == 32) {
-            tmem_ld32(t_row + c, ra);
-            tmem_ld32(t_row + HALF + c, rg);
-          } else {
-            uint32_t t16a[16], t16g[16];
-            tmem_ld16(t_row + c, t16a);
-            tmem_ld16(t_row + HALF + c, t16g);
+        for (int c = eh * CH; c < BN; c += kSplit * CH) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          const int nb = n0 + c;  // packed column of the chunk
+          float4 b[8];
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) { ra[j] = t16a[j]; rg[j] = t16g[j]; }
-          }
-          // value / gate biases, one 8-column group ahead of its use (the first group's fetched
-          // while the TMEM load is in flight)
-          auto ldb = [&](int col, float4 (&b)[4]) {
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4* bv = reinterpret_cast<const float4*>(p.bias + n0 + col);
-            const float4* bg = reinterpret_cast<const float4*>(p.bias + n0 + HALF + col);
-            b[0] = p.bias ? __ldg(bv) : z;
-            b[1] = p.bias ? __ldg(bv + 1) : z;
-            b[2] = p.bias ? __ldg(bg) : z;
-            b[3] = p.bias ? __ldg(bg + 1) : z;
-          };
-          float4 bcur[4], bnext[4];
-          ldb(c, bcur);
+          for (int q = 0; q < 8; ++q) b[q] = p.bias ? __ldg(reinterpret_cast<const float4*>(p.bias + nb) + q) : z;
           tmem_wait_ld();
-          const int nc = nout0 + c;
+          const int nc = nb / 2;
           if (mvalid && nc < p.N / 2) {
+            const float* bf = reinterpret_cast<const float*>(b);
+            float v[16];
 #pragma unroll
-            for (int g = 0; g < CH / 8; ++g) {
-              if (g + 1 < CH / 8) ldb(c + (g + 1) * 8, bnext);
-              const float bav[8] = {bcur[0].x, bcur[0].y, bcur[0].z, bcur[0].w, bcur[1].x, bcur[1].y, bcur[1].z, bcur[1].w};
-              const float bgv[8] = {bcur[2].x, bcur[2].y, bcur[2].z, bcur[2].w, bcur[3].x, bcur[3].y, bcur[3].z, bcur[3].w};
-              float v[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int cj = c + g * 8 + j;
-                float a = __uint_as_float(ra[g * 8 + j]), gt = __uint_as_float(rg[g * 8 + j]);
-                if (p.wscale) {
-                  a *= __ldg(p.wscale + n0 + cj);
-                  gt *= __ldg(p.wscale + n0 + HALF + cj);
-                }
-                if (p.ln_stat) {  // folded LayerNorm (see epi_apply)
-                  a = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + n0 + cj), a);
-                  gt = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + n0 + HALF + cj), gt);
-                }
-                a += bav[j];
-                gt += bgv[j];
-                v[j] = a * gelu_as(gt);
+            for (int j = 0; j < 16; ++j) {
+              float a = __uint_as_float(r[j]), gt = __uint_as_float(r[16 + j]);
+              if (p.wscale) {
+                a *= __ldg(p.wscale + nb + j);
+                gt *= __ldg(p.wscale + nb + 16 + j);
               }
-              *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc + g * 8) = pack8(v);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) bcur[q] = bnext[q];
+              if (p.ln_stat) {  // folded LayerNorm (see epi_apply)
+                a = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + nb + j), a);
+                gt = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + nb + 16 + j), gt);
+              }
+              v[j] = (a + bf[j]) * gelu_as(gt + bf[16 + j]);
             }
+            float lo[8], hi[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { lo[j] = v[j]; hi[j] = v[8 + j]; }
+            uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + nc);
+            dst[0] = pack8(lo);
+            dst[1] = pack8(hi);
           }
+        }
         }
       } else {
 #pragma unroll 1
@@ -994,7 +971,7 @@ TileChoice choose_tiles(const GemmArgs& a, bool allow_ws = true) {
     const int bn = tcst.bn;
     if (a.N % bn != 0 || (tcst.pair && !pair_ok)) continue;
     if (w8 && bn == 192) continue;                  // wo8 tiles: 64 / 128 / 160 / 256
-    if (a.epi == kEpiGeglu && bn != 256) continue;  // value/gate halves live in one 256-wide tile
+    if (a.epi == kEpiGeglu && bn % 32) continue;  // whole 16 value + 16 gate row groups per tile
     const int tiles = (tcst.pair ? (a.M + 2 * BM - 1) / (2 * BM) : (a.M + BM - 1) / BM) * (a.N / bn);
     const int teams = tcst.pair ? sms / 2 : sms;
     const int max_split = (a.epi == kEpiNchwF32 || a.epi == kEpiGeglu) ? 1 : std::max(1, std::min(32, KB / 3));
@@ -1060,7 +1037,8 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   if (tc.splits > 1 && (a.ws == nullptr || a.ws_bytes < (size_t)tc.splits * a.M * a.N * sizeof(float)))
     tc = choose_tiles(a, false);  // no workspace: single pass or cluster split
   const int bn = tc.bn;
-  if (a.epi == kEpiGeglu && (a.N % bn != 0)) return cudaErrorInvalidValue;
+  if (a.epi == kEpiGeglu && (a.N % bn != 0 || bn % 32 != 0 || (a.ld_out ? a.ld_out : a.N / 2) % 8))
+    return cudaErrorInvalidValue;
   if (a.epi == kEpiHeads && (a.head_d % 8 != 0 || a.head_C % 8 != 0 || a.head_dp < a.head_d ||
                              (a.head_vt >= 0 && (a.head_d16 < a.head_d || a.head_spad < a.rows_per_image))))
     return cudaErrorInvalidValue;

@@ -10,7 +10,7 @@ namespace sdg {
 
 enum EpiMode : int {
   kEpiPlain = 0,    // out[m, n] fp16 (row stride ld_out)
-  kEpiGeglu = 1,    // tile holds [a | gate] column halves; out[m, n/2-space] = a * gelu(gate)
+  kEpiGeglu = 1,    // W rows interleave 16 value and 16 gate rows; out[m, n/2] = value * gelu(gate)
   kEpiHeads = 2,    // scatter into padded per-head layout [B*heads, S, dp] (Q/K/V for attention)
   kEpiNchwF32 = 3,  // out_f32[b, n, p] fp32 (final conv_out)
 };

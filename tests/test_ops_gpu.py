@@ -57,8 +57,8 @@ def test_linear(sdg, cuda, gen, M, N, K, bias, resid, act):
     assert rel(y, ref) < TOL
 
 
-def test_linear_geglu(sdg, cuda, gen):
-    M, C = 4096, 320
+@pytest.mark.parametrize("M,C", [(4096, 320), (2048, 640), (512, 1280), (200, 320)])  # the UNet's FF-proj shapes
+def test_linear_geglu(sdg, cuda, gen, M, C):
     x = rnd(M, C, g=gen).half()
     w = rnd(8 * C, C, std=1 / math.sqrt(C), g=gen).half()
     b = rnd(8 * C, std=0.1, g=gen).float()
