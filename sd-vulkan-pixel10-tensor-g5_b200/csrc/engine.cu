@@ -56,10 +56,7 @@ struct HostWeight {
   std::string file;  // the <key>.bin it was read from (sdg_load_dir), empty when uploaded from memory
 };
 // fp16 weights (w), or weight-only int8 (w8 + per-row scale ws) after sdg_quantize_wo8
-struct Lin {
-  __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; int8_t* w8 = nullptr; float* ws = nullptr;
-  float* csum = nullptr;  // LayerNorm folded in (gamma in w, beta in b): per-row sum of the effective weights
-};
+struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; int8_t* w8 = nullptr; float* ws = nullptr; };
 struct Norm { float* g = nullptr; float* b = nullptr; int C = 0; };
 struct ConvW {
   __half* w = nullptr; float* b = nullptr; int Co = 0, Ci = 0, k = 3; int8_t* w8 = nullptr; float* ws = nullptr;
@@ -266,7 +263,6 @@ struct WeightPacker {
     int rows, cols;
     __half** w16;
     int8_t** w8;
-    size_t csum_off = 0;  // folded LayerNorm: per-row weight sums, recomputed after quantisation
   };
   std::vector<Mat> mats;
   std::string missing;
@@ -276,7 +272,7 @@ struct WeightPacker {
   void mat(size_t off, int rows, int cols, __half** w16, int8_t** w8, float** ws) {
     const size_t so = reserve((size_t)rows * 4);
     place(ws, so);
-    mats.push_back({off, so, rows, cols, w16, w8, 0});
+    mats.push_back({off, so, rows, cols, w16, w8});
   }
   // Weight-only int8 (the reference's wo8 scheme, tools/quantize_wo8.py:42-46 via
   // ai-edge-quantizer weight_only_wi8_afp32): per output row, symmetric, narrow range,
@@ -298,15 +294,11 @@ struct WeightPacker {
         float s16 = __half2float(__float2half_rn(mx / 127.f));
         if (s16 == 0.f) s16 = 1.f;
         sc[r] = s16;
-        double qsum = 0.0;
         for (int c = 0; c < m.cols; ++c) {
           float q = std::nearbyint(row[c] / s16);
           q = std::min(127.f, std::max(-127.f, q));
           dst[(size_t)r * m.cols + c] = static_cast<int8_t>(q);
-          qsum += q;
         }
-        // folded LayerNorm: the row sum of the weights the GEMM actually uses (q * scale)
-        if (m.csum_off) reinterpret_cast<float*>(staging.data() + m.csum_off)[r] = (float)(qsum * s16);
       }
     }
   }
@@ -342,50 +334,10 @@ struct WeightPacker {
     float* f = reinterpret_cast<float*>(staging.data() + o);
     for (int i = 0; i < n; ++i) f[i] = hw ? h2f(hw->data[i]) : 0.f;
   }
-  // staging offsets of the last norm() call's gamma and beta
-  size_t last_g = 0, last_b = 0;
   void norm(Norm& nm, const std::string& pf, int C) {
     nm.C = C;
     vecf(&nm.g, pf + ".weight", C);
-    last_g = fixups.back().first;
     vecf(&nm.b, pf + ".bias", C);
-    last_b = fixups.back().first;
-  }
-  // LayerNorm (gamma at g_off, beta at b_off, C values each) followed by the linear L (rows [N][K = C] at
-  // w_off, bias at b_lin_off or none): fold the affine part into the linear,
-  //   LN(x) . W^T + b = rstd * (x - mean) . (W * gamma)^T + (b + W . beta),
-  // so W <- fp16(W * gamma) (row-wise along K), b <- b + W . beta, and csum[n] = sum_k W'[n, k] (the
-  // GEMM applies rstd * (acc - mean * csum) when it reads the raw rows). The norm keeps gamma = 1,
-  // beta = 0, so a plain LayerNorm launch (where the fold is not used) only normalises.
-  void fold_ln(Lin& L, size_t w_off, size_t b_lin_off, size_t g_off, size_t b_off) {
-    const int N = L.N, K = L.K;
-    if (!b_lin_off) {
-      b_lin_off = reserve((size_t)N * 4);
-      place(&L.b, b_lin_off);
-      std::memset(staging.data() + b_lin_off, 0, (size_t)N * 4);
-    }
-    const size_t cs_off = reserve((size_t)N * 4);
-    place(&L.csum, cs_off);
-    for (Mat& m : mats)
-      if (m.off == w_off) m.csum_off = cs_off;
-    uint16_t* w = reinterpret_cast<uint16_t*>(staging.data() + w_off);
-    float* bias = reinterpret_cast<float*>(staging.data() + b_lin_off);
-    float* cs = reinterpret_cast<float*>(staging.data() + cs_off);
-    float* g = reinterpret_cast<float*>(staging.data() + g_off);
-    float* be = reinterpret_cast<float*>(staging.data() + b_off);
-    for (int n = 0; n < N; ++n) {
-      double sb = 0.0, sc = 0.0;
-      for (int k = 0; k < K; ++k) {
-        const float wf = h2f(w[(size_t)n * K + k]);
-        sb += (double)wf * be[k];
-        const __half h = __float2half_rn(wf * g[k]);
-        w[(size_t)n * K + k] = __half_as_ushort(h);
-        sc += (double)__half2float(h);
-      }
-      bias[n] += (float)sb;
-      cs[n] = (float)sc;
-    }
-    for (int k = 0; k < K; ++k) { g[k] = 1.f; be[k] = 0.f; }
   }
   // Linear stored [in,out] in the reference format -> [out][in] rows placed at row offset `row0` of `dst_o`.
   void linear_rows(size_t dst_o, int row0, int ld, const std::string& k, int in, int out) {
@@ -472,11 +424,8 @@ int Engine::prepare() {
     P.norm(t.gn, pf + ".norm", C);
     P.conv1x1_as_linear(t.pin, pf + ".proj_in", C, C);
     P.norm(t.ln1, b + ".norm1", C);
-    const size_t g1 = P.last_g, b1 = P.last_b;
     P.norm(t.ln2, b + ".norm2", C);
-    const size_t g2 = P.last_g, b2 = P.last_b;
     P.norm(t.ln3, b + ".norm3", C);
-    const size_t g3 = P.last_g, b3 = P.last_b;
     {  // fused QKV [3C][C]
       t.qkv.N = 3 * C; t.qkv.K = C;
       size_t o = P.reserve((size_t)3 * C * C * 2);
@@ -485,11 +434,9 @@ int Engine::prepare() {
       P.linear_rows(o, 0, C, b + ".attn1.to_q.weight", C, C);
       P.linear_rows(o, C, C, b + ".attn1.to_k.weight", C, C);
       P.linear_rows(o, 2 * C, C, b + ".attn1.to_v.weight", C, C);
-      P.fold_ln(t.qkv, o, 0, g1, b1);
     }
     P.linear(t.out1, b + ".attn1.to_out.0", C, C, true);
     P.linear(t.q2, b + ".attn2.to_q", C, C, false);
-    P.fold_ln(t.q2, P.mats.back().off, 0, g2, b2);
     {  // fused cross K/V [2C][768]
       t.kv2.N = 2 * C; t.kv2.K = kCtxDim;
       size_t o = P.reserve((size_t)2 * C * kCtxDim * 2);
@@ -519,7 +466,6 @@ int Engine::prepare() {
         memcpy(dst + (size_t)r * C, src + (size_t)srow * C, (size_t)C * 2);
         bd[r] = hb ? h2f(hb->data[srow]) : 0.f;
       }
-      P.fold_ln(t.ff1, o, bo, g3, b3);
     }
     P.linear(t.ff2, b + ".ff.net.2", 4 * C, C, true);
     P.conv1x1_as_linear(t.pout, pf + ".proj_out", C, C);
@@ -768,14 +714,11 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   __half* hn = alloc_h((size_t)M * C);
   __half* o = alloc_h((size_t)M * C);
   __half* gg = alloc_h((size_t)M * 4 * C);
-  auto lin_args = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
+  auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
     GemmArgs a;
     a.M = M; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b; a.residual = resid;
     a.out = y;
-    return a;
-  };
-  auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
-    gemm(lin_args(A, K, L, resid, y), kCatGemm);
+    gemm(a, kCatGemm);
   };
   auto ln = [&](const __half* xin, const Norm& n) {
     cat_bytes[kCatLN] += 2.0 * 2.0 * M * C;
@@ -784,30 +727,15 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
       return launch_layernorm(xin, M, C, g, b, kLnEps, hn, s);
     }, "layernorm M=" + std::to_string(M) + " C=" + std::to_string(C), 0.0, 2.0 * 2.0 * M * C);
   };
-  auto heads_args = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1,
-                        __half* o2, int vt_idx, int spad) {
+  auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
+                   int vt_idx, int spad) {
     GemmArgs a;
     a.M = Mr; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b;
     a.epi = kEpiHeads; a.rows_per_image = rows_per_image;
     a.head_out[0] = o0; a.head_out[1] = o1; a.head_out[2] = o2;
     a.head_C = C; a.heads = kHeads; a.head_d = d; a.head_dp = dp;
     a.head_vt = vt_idx; a.head_d16 = d16; a.head_spad = spad;
-    return a;
-  };
-  // LayerNorm folded into its producer (per-row chunk statistics of the stored outputs) and its
-  // consumer (reads the raw rows; gamma / beta are folded into its weights and bias) when both
-  // GEMMs run single-pass; otherwise a LayerNorm launch (normalise only) between them.
-  const int nch = C / 32;
-  float2* lnst = static_cast<float2*>(alloc((size_t)M * nch * sizeof(float2)));
-  auto single_pass = [&](const GemmArgs& a) {
-    const GemmPlan pl = gemm_plan(a, true);
-    return pl.splits == 1 && pl.csplit == 1 && pl.bn >= 32;
-  };
-  auto fold = [&](GemmArgs& prod, GemmArgs& cons, const Lin& L) {
-    if (!L.csum || C % 64 || !single_pass(prod) || !single_pass(cons)) return false;
-    prod.rowstat_out = lnst; prod.rowstat_ld = nch;
-    cons.ln_stat = lnst; cons.ln_nchunk = nch; cons.ln_csum = L.csum; cons.ln_eps = kLnEps;
-    return true;
+    gemm(a, kCatGemm);
   };
   auto attn = [&](const __half* q, const __half* k, const __half* vt, int Sk, int vt_ld) {
     cat_flops[kCatAttn] += 4.0 * B * kHeads * (double)S * Sk * d;
@@ -820,24 +748,14 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
               " d=" + std::to_string(d),
           4.0 * B * kHeads * (double)S * Sk * d);
   };
+  lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
+  ln(tt, t.ln1);
   const int spad = (S + 7) / 8 * 8;                                // V^T rows are 16-byte multiples
-  {
-    GemmArgs pa = lin_args(g, C, t.pin, nullptr, tt);              // proj_in (1x1)
-    GemmArgs ca = heads_args(tt, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, spad);  // Q, K, V^T of norm1(t)
-    const bool f = fold(pa, ca, t.qkv);
-    gemm(pa, kCatGemm);
-    if (!f) { ln(tt, t.ln1); ca.a0 = hn; }
-    gemm(ca, kCatGemm);
-  }
+  heads(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, spad);         // Q, K, V^T
   attn(ab.q, ab.k, ab.vt, S, spad);                                // self-attention
-  {
-    GemmArgs pa = lin_args(o, C, t.out1, tt, tt);                  // t += to_out(attn)
-    GemmArgs ca = heads_args(tt, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);  // Q (cross) of norm2(t)
-    const bool f = fold(pa, ca, t.q2);
-    gemm(pa, kCatGemm);
-    if (!f) { ln(tt, t.ln2); ca.a0 = hn; }
-    gemm(ca, kCatGemm);
-  }
+  lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
+  ln(tt, t.ln2);
+  heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
   if (!ctx_cached) {  // K, V^T from the context: issued on the side stream at the start of the forward
     if (ci < (int)kv_ready_.size())
       join(kv_ready_[ci]);
@@ -845,14 +763,12 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
       ctx_kv(t, cb);
   }
   attn(ab.q, cb.k, cb.vt, kCtxLen, kCtxPad);                       // cross-attention
+  lin(o, C, t.out2, tt, tt);
+  ln(tt, t.ln3);
   {
-    GemmArgs pa = lin_args(o, C, t.out2, tt, tt);                  // t += to_out(cross-attn)
-    GemmArgs a;                                                    // GEGLU FF-proj of norm3(t)
-    a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = tt; a.cin0 = C; set_w(a, t.ff1.w, t.ff1.w8, t.ff1.ws); a.bias = t.ff1.b;
+    GemmArgs a;
+    a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = hn; a.cin0 = C; set_w(a, t.ff1.w, t.ff1.w8, t.ff1.ws); a.bias = t.ff1.b;
     a.epi = kEpiGeglu; a.out = gg; a.ld_out = 4 * C;
-    const bool f = fold(pa, a, t.ff1);
-    gemm(pa, kCatGemm);
-    if (!f) { ln(tt, t.ln3); a.a0 = hn; }
     gemm(a, kCatGemm);
   }
   lin(gg, 4 * C, t.ff2, tt, tt);                                   // t += ff(t)

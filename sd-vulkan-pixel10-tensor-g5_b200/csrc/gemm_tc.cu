@@ -69,12 +69,6 @@ struct GemmDev {
   float* ws;                 // [splits][M][N] fp32 partials when splits > 1
   const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
-  float2* rowstat_out;       // folded LayerNorm, producer side: per (row, 32-column chunk) (mean, M2)
-  int rowstat_ld;
-  const float2* ln_stat;     // folded LayerNorm, consumer side (see GemmArgs)
-  int ln_nchunk;
-  const float* ln_csum;
-  float ln_eps;
   int stall_it;              // failure-path test: k-block iteration whose stage is never loaded (-1: none)
   unsigned long long wait_ns;  // limit of every bounded wait
 };
@@ -246,53 +240,8 @@ __device__ __forceinline__ void epi_load(const GemmDev& p, int m, int img, int n
 
 // Fused epilogue of one chunk (plain or attention-head outputs) from the accumulator words r and
 // the prefetched operands; same arithmetic as epilogue8.
-// Folded LayerNorm, consumer side: (mean, rstd) of row m from its C/32 chunk pairs (mean_i, M2_i),
-// all over 32 values: one pass about the first chunk's mean, M2 = sum M2_i + 32 (S2 - S1^2 / P).
-__device__ __forceinline__ float2 ln_row_stats(const GemmDev& p, int m, bool mvalid) {
-  if (!mvalid) return make_float2(0.f, 0.f);
-  const float4* src = reinterpret_cast<const float4*>(p.ln_stat + (size_t)m * p.ln_nchunk);
-  const float4 f0 = __ldg(src);
-  const float shift = f0.x;
-  float s1 = 0.f, s2 = 0.f, m2 = 0.f;
-  for (int i = 0; i < p.ln_nchunk / 2; ++i) {
-    const float4 f = i == 0 ? f0 : __ldg(src + i);
-    const float d0 = f.x - shift, d1 = f.z - shift;
-    s1 += d0 + d1;
-    s2 = fmaf(d0, d0, fmaf(d1, d1, s2));
-    m2 += f.y + f.w;
-  }
-  const float P = (float)p.ln_nchunk;
-  const float var = fmaxf(m2 + 32.f * (s2 - s1 * s1 / P), 0.f) / (32.f * P);
-  return make_float2(shift + s1 / P, rsqrtf(var + p.ln_eps));
-}
-
-// Folded LayerNorm, producer side: (mean, M2) of the chunk's 32 stored fp16 values (four packed uint4).
-__device__ __forceinline__ void rowstat_store(const GemmDev& p, int m, int n, const uint4 (&pk)[4]) {
-  float x[32];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const __half2* h = reinterpret_cast<const __half2*>(&pk[q]);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h[e]);
-      x[8 * q + 2 * e] = f.x;
-      x[8 * q + 2 * e + 1] = f.y;
-    }
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) s += x[i];
-  const float mu = s * (1.f / 32.f);
-  float m2 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) m2 = fmaf(x[i] - mu, x[i] - mu, m2);
-  p.rowstat_out[(size_t)m * p.rowstat_ld + n / 32] = make_float2(mu, m2);
-}
-
 template <int CH>
-__device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int n, const uint32_t* r, const EpiIn<CH>& in,
-                                          float2 ln = make_float2(0.f, 0.f)) {
-  uint4 pk[CH / 8];  // the chunk's stored values (folded LayerNorm producer)
+__device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int n, const uint32_t* r, const EpiIn<CH>& in) {
 #pragma unroll
   for (int g = 0; g < CH / 8; ++g) {
     const int ng = n + g * 8;
@@ -303,13 +252,6 @@ __device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int 
     if (p.wscale) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + min(ng + j, p.N - 1));
-    }
-    if (p.ln_stat) {  // rstd * (x.w - mean * sum(w)) = LayerNorm(x).w (gamma folded into w)
-      const float4 c0 = __ldg(reinterpret_cast<const float4*>(p.ln_csum + ng));
-      const float4 c1 = __ldg(reinterpret_cast<const float4*>(p.ln_csum + ng) + 1);
-      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = ln.y * fmaf(-ln.x, cs[j], v[j]);
     }
     const float4 b0 = in.b[2 * g], b1 = in.b[2 * g + 1];
     v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
@@ -344,11 +286,7 @@ __device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int 
       *reinterpret_cast<uint4*>(dst) = pack8(v);
       continue;
     }
-    pk[g] = pack8(v);
-    *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + ng) = pk[g];
-  }
-  if constexpr (CH == 32) {
-    if (p.rowstat_out) rowstat_store(p, m, n, pk);
+    *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + ng) = pack8(v);
   }
 }
 
@@ -642,8 +580,6 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       uint4 res_next[C::kChunk / 8];
       const bool fused_res = csp == 1 && p.splits == 1 && p.epi != kEpiNchwF32 && p.epi != kEpiGeglu && p.residual;
       if (fused_res) res_load<C::kChunk>(p, m, n0 + eh * C::kChunk, mvalid, res_next);
-      // folded LayerNorm: this row's (mean, rstd), computed while the main loop runs
-      const float2 ln = p.ln_stat ? ln_row_stats(p, m, mvalid) : make_float2(0.f, 0.f);
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc, p.wait_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -677,10 +613,6 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
               if (p.wscale) {
                 a *= __ldg(p.wscale + nb + j);
                 gt *= __ldg(p.wscale + nb + 16 + j);
-              }
-              if (p.ln_stat) {  // folded LayerNorm (see epi_apply)
-                a = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + nb + j), a);
-                gt = ln.y * fmaf(-ln.x, __ldg(p.ln_csum + nb + 16 + j), gt);
               }
               v[j] = (a + bf[j]) * gelu_as(gt + bf[16 + j]);
             }
@@ -718,7 +650,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           tmem_wait_ld();
           if (!mvalid || n >= p.N) continue;
           if (fused) {
-            epi_apply<CH>(p, m, img, n, r, in, ln);
+            epi_apply<CH>(p, m, img, n, r, in);
             continue;
           }
           if (p.splits > 1) {
@@ -1061,14 +993,6 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
   d.stall_it = a.test_stall_iter;
-  d.rowstat_out = a.rowstat_out; d.rowstat_ld = a.rowstat_ld;
-  d.ln_stat = a.ln_stat; d.ln_nchunk = a.ln_nchunk; d.ln_csum = a.ln_csum; d.ln_eps = a.ln_eps;
-  if ((a.rowstat_out || a.ln_stat) && (tc.splits > 1 || tc.csplit > 1 || bn < 32)) return cudaErrorInvalidValue;
-  if (a.rowstat_out && (a.epi != kEpiPlain || a.N % 32 || a.rowstat_ld < a.N / 32)) return cudaErrorInvalidValue;
-  if (a.ln_stat && (!a.ln_csum || a.ln_nchunk <= 0 || a.ln_nchunk % 2 || a.K != 32 * a.ln_nchunk ||
-                    (reinterpret_cast<uintptr_t>(a.ln_stat) & 15) || (reinterpret_cast<uintptr_t>(a.ln_csum) & 15) ||
-                    a.epi == kEpiNchwF32))
-    return cudaErrorInvalidValue;
   d.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kWaitTimeoutNs;
   if (a.w8 && !a.wscale) return cudaErrorInvalidValue;
   // the epilogue reads bias / per-image bias 8 columns at a time as two float4

@@ -49,18 +49,6 @@ struct GemmArgs {
   int head_C = 0, heads = 0, head_d = 0, head_dp = 0;
   int head_vt = -1;                 // index of the output stored transposed [BH, d16, head_spad]
   int head_d16 = 0, head_spad = 0;
-  // LayerNorm folded into the GEMMs on either side of it (single-pass plans only):
-  //  producer: rowstat_out[m * rowstat_ld + n / 32] = (mean, M2) of the 32 fp16 outputs of row m in
-  //            columns [n, n + 32) (exact, about the chunk's own mean)
-  //  consumer: A holds the raw (un-normalised) rows; ln_stat [m * ln_nchunk + j] are those chunk
-  //            pairs; W holds W * gamma, bias holds bias + W * beta, ln_csum[n] = sum_k (W * gamma)[n, k];
-  //            the epilogue applies rstd * (acc - mean * ln_csum[n]) before the bias
-  float2* rowstat_out = nullptr;
-  int rowstat_ld = 0;
-  const float2* ln_stat = nullptr;
-  int ln_nchunk = 0;
-  const float* ln_csum = nullptr;
-  float ln_eps = 0.f;
   int bn = 0;                       // tile N (0 = choose)
   float* ws = nullptr;              // split-K workspace (fp32); split-K only when large enough
   size_t ws_bytes = 0;

@@ -105,6 +105,29 @@ def test_unet_forward_matches_oracle(engine, unet_weights, B, H):
     assert err < UNET_TOL
 
 
+def test_unet_layernorm_affine_folded(sdg, cuda, unet_weights):
+    """Default init leaves every LayerNorm at gamma = 1, beta = 0, so the other full-UNet cases never
+    exercise the LayerNorm affine; here the transformer LayerNorms get random gamma and beta."""
+    g = torch.Generator().manual_seed(21)
+    w = dict(unet_weights)
+    for k, v in unet_weights.items():
+        if ".transformer_blocks.0.norm" in k:
+            noise = torch.randn(v.shape, generator=g) * 0.3
+            w[k] = ((1.0 + noise) if k.endswith(".weight") else noise).half()
+    e = sdg.Engine(0)
+    try:
+        e.upload_weights(W.iter_reference_blobs(w))
+        e.prepare()
+        lat, t, ctx = W.make_inputs(2, 64, 64, seed=22)
+        got = e.forward(lat.numpy(), t.numpy(), ctx.numpy())
+    finally:
+        e.release()
+    ref = oracle_forward(w, lat, t, ctx)
+    err = rel(got, ref)
+    print(f"UNet B=2 64x64, LayerNorm affines: relErr {err:.3e}")
+    assert np.isfinite(got).all() and err < UNET_TOL
+
+
 def test_unet_shared_timestep_and_tproj_entry(engine):
     lat, t, ctx = W.make_inputs(2, 32, 32, seed=5)
     a = engine.forward(lat.numpy(), np.array([999.0], np.float32), ctx.numpy())
