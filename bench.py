@@ -35,11 +35,12 @@ METRIC = "UNet fwd/s (B=2 CFG, 64×64 latent) at 1/2/4/8 B200; % dense-fp16 tens
 UNIT = "fwd/s"
 B, H, W = 2, 64, 64
 FLOPS_PER_FWD = 1.606e12          # algorithmic FLOPs per B=2 64x64 forward (direct-conv count)
-# DRAM bytes (read + write) of one conv3x3 launch at 64x64x320, B=2, from one ncu capture
-# (--set full capture of opbench's conv3x3_320_64); algorithmic bytes of that launch: 12.3 MB
-CONV_TRAFFIC_PER_LAUNCH = 12.80e6
-CONV_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 64x64x320 conv3x3 launch "
-                     "(the most frequent conv3x3 shape), bytes per launch")
+# DRAM bytes (read + write) per gemm_tc_kernel launch, averaged over the 210 GEMM launches (and 17 split-K
+# reduce launches) of one B=2 64x64 forward, from a one-pass ncu launch list of this bench
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/forward_launches_b2_64x64.md): 2.85 GB per forward
+GEMM_TRAFFIC_PER_LAUNCH = 13.56e6
+GEMM_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of every GEMM launch of one forward "
+                     "(split-K reduce launches included) / 210 GEMM launches; serialised replay, cold caches")
 L2_FLUSH_BYTES = 256 << 20        # > 126 MB L2
 
 
@@ -370,14 +371,15 @@ def main():
             cats[c] = eng.profile_category(c, B, H, W, reps=10)
         except sdg.SdgError:
             pass
-    g_ms, g_n, g_fl, _ = cats["CONV3+GEMM"]
+    g_ms, g_n, g_fl, g_by = cats["CONV3+GEMM"]
     achieved = g_fl / (g_ms / 1000.0) / 1e12
     roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel: every conv3x3 / conv1x1 / linear launch of the forward",
                 "achieved": achieved, "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved / tc_burst,
                 "peak_source": f"{src} bf16_tflops (burst)",
                 "timing": "the forward's GEMM launches replayed alone as a CUDA graph (CUDA events around 10 "
                           "replays), ms per forward " + f"{g_ms:.4f}",
-                "traffic": CONV_TRAFFIC_PER_LAUNCH, "traffic_note": CONV_TRAFFIC_NOTE,
+                "traffic": GEMM_TRAFFIC_PER_LAUNCH, "traffic_note": GEMM_TRAFFIC_NOTE,
+                "algorithmic_bytes_per_launch": g_by / max(g_n, 1),
                 "launches_per_fwd": g_n, "flops_per_launch": g_fl / max(g_n, 1),
                 "whole_forward_tflops": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12,
                 "whole_forward_frac_of_sustained": FLOPS_PER_FWD / (ms_per_step / 1000.0) / 1e12 / tc_sust,

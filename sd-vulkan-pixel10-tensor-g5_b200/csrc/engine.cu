@@ -601,8 +601,20 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
         0.0, 2.0 * 2.0 * B * HW * (x.C + (x2 ? x2->C : 0)));
 }
 
+// Algorithmic HBM bytes of one GEMM: its input activation once (a 3x3 convolution's input, not the
+// nine taps), the weights, the output and the residual.
+static double gemm_algorithmic_bytes(const GemmArgs& a) {
+  const double cin = a.cin0 + a.cin1;
+  const double in = 2.0 * a.M * (a.taps == 9 ? cin : (double)a.K);
+  const double wt = (a.w8 ? 1.0 : 2.0) * a.N * a.K + (a.w8 ? 4.0 * a.N : 0.0);
+  const double out = a.epi == kEpiNchwF32 ? 4.0 * a.M * a.N : 2.0 * a.M * (a.epi == kEpiGeglu ? a.N / 2 : a.N);
+  const double res = a.residual ? 2.0 * a.M * a.N : 0.0;
+  return in + wt + out + res;
+}
+
 void Builder::gemm(GemmArgs a, int cat) {
   cat_flops[cat] += 2.0 * a.M * a.N * a.K;
+  cat_bytes[cat] += gemm_algorithmic_bytes(a);
   const size_t mark = off_;  // split-K workspace lives only until the GEMM's reduce pass
   a.ws_bytes = on_side_ ? 0 : gemm_workspace_bytes(a);
   a.ws = a.ws_bytes ? alloc_f(a.ws_bytes / 4) : nullptr;
@@ -621,7 +633,8 @@ void Builder::gemm(GemmArgs a, int cat) {
     lb[0] = 0;
   }
   issue(cat, cat == kCatConv3 ? "conv3x3" : "gemm", gemm_launch_count(a),
-        [a, err = pl_.dev_err](cudaStream_t s) { return launch_gemm(a, err, s); }, lb, 2.0 * a.M * a.N * a.K);
+        [a, err = pl_.dev_err](cudaStream_t s) { return launch_gemm(a, err, s); }, lb, 2.0 * a.M * a.N * a.K,
+        gemm_algorithmic_bytes(a));
   off_ = mark;
 }
 
