@@ -227,15 +227,15 @@ __device__ __forceinline__ void epi_load(const GemmDev& p, int m, int img, int n
     in.b[q] = (ok && p.bias) ? __ldg(reinterpret_cast<const float4*>(p.bias + n) + q) : z;
   }
   if (p.rowbias) {  // resnet conv1: the time-embedding projection per image
+    const int im = mvalid ? img : 0;  // rows past M (last partial tile) must not index past the last image
 #pragma unroll
     for (int q = 0; q < CH / 4; ++q) {
       if (n + 4 * q >= p.N) break;
-      const float4 t = __ldg(reinterpret_cast<const float4*>(p.rowbias + (size_t)img * p.rowbias_ld + n) + q);
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p.rowbias + (size_t)im * p.rowbias_ld + n) + q);
       in.b[q].x += t.x; in.b[q].y += t.y; in.b[q].z += t.z; in.b[q].w += t.w;
     }
   }
   (void)m;
-  (void)mvalid;
 }
 
 // Fused epilogue of one chunk (plain or attention-head outputs) from the accumulator words r and
@@ -288,6 +288,77 @@ __device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int 
     }
     *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + ng) = pack8(v);
   }
+}
+
+// 4x4 transpose of 16-byte blocks within each quad of lanes: on return, lane 4g + j holds in b[i]
+// what lane 4g + i held in b[j]. Two pairwise exchanges (lane ^ 1, then lane ^ 2), each swapping the
+// two blocks whose index bit differs from the lane's bit; register-only (selects, no local memory).
+__device__ __forceinline__ uint4 sel4(bool c, const uint4& a, const uint4& b) {
+  return make_uint4(c ? a.x : b.x, c ? a.y : b.y, c ? a.z : b.z, c ? a.w : b.w);
+}
+__device__ __forceinline__ uint4 shfl_xor4(const uint4& v, int m) {
+  return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
+                    __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
+}
+__device__ __forceinline__ void quad_transpose(uint4 (&b)[4], int lane) {
+  {  // stage 1 (partner lane ^ 1): blocks {0,1} and {2,3}; a lane with bit 0 set swaps out 0 and 2
+    const bool hi = lane & 1;
+    const uint4 w0 = shfl_xor4(sel4(hi, b[0], b[1]), 1);
+    const uint4 w1 = shfl_xor4(sel4(hi, b[2], b[3]), 1);
+    b[0] = sel4(hi, w0, b[0]); b[1] = sel4(hi, b[1], w0);
+    b[2] = sel4(hi, w1, b[2]); b[3] = sel4(hi, b[3], w1);
+  }
+  {  // stage 2 (partner lane ^ 2): blocks {0,2} and {1,3}; a lane with bit 1 set swaps out 0 and 1
+    const bool hi = lane & 2;
+    const uint4 w0 = shfl_xor4(sel4(hi, b[0], b[2]), 2);
+    const uint4 w1 = shfl_xor4(sel4(hi, b[1], b[3]), 2);
+    b[0] = sel4(hi, w0, b[0]); b[2] = sel4(hi, b[2], w0);
+    b[1] = sel4(hi, w1, b[1]); b[3] = sel4(hi, b[3], w1);
+  }
+}
+
+// Plain fused epilogue of one 32-column chunk with coalesced stores: each thread computes its own
+// row's 32 outputs (four 16-byte blocks), a quad transpose hands lane 4g + j block j of rows
+// 4g .. 4g + 3, and each of four stores writes eight rows x 64 contiguous bytes (instead of 32 rows x
+// 16 bytes). Called by all 32 lanes of the warp (rows >= M compute on zero residual, store nothing).
+__device__ __forceinline__ void epi_apply_rows(const GemmDev& p, int m, int img, int n, const uint32_t* r,
+                                               const EpiIn<32>& in, int lane) {
+  uint4 b[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+    if (p.wscale) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + n + g * 8 + j);
+    }
+    const float4 b0 = in.b[2 * g], b1 = in.b[2 * g + 1];
+    v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+    v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+    if (p.residual) {
+      const __half2* h = reinterpret_cast<const __half2*>(&in.res[g]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        v[2 * e] += f.x;
+        v[2 * e + 1] += f.y;
+      }
+    }
+    if (p.act == 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+    }
+    b[g] = pack8(v);
+  }
+  quad_transpose(b, lane);
+  const int row0 = m - lane + (lane & ~3);  // first row of this lane's quad
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int mr = row0 + i;
+    if (mr < p.M) *reinterpret_cast<uint4*>(p.out + (size_t)mr * p.ld_out + n + 8 * (lane & 3)) = b[i];
+  }
+  (void)img;
 }
 
 // int8 x4 (one 32-bit word) -> two fp16x2, exact: bias the bytes to unsigned,
@@ -648,7 +719,14 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
             if (c + kSplit * CH < BN) res_load<CH>(p, m, n + kSplit * CH, mvalid, res_next);  // next chunk's
           }
           tmem_wait_ld();
-          if (!mvalid || n >= p.N) continue;
+          if (n >= p.N) continue;  // (the same for every lane of the warp)
+          if constexpr (CH == 32) {
+            if (fused && p.epi == kEpiPlain) {  // all 32 lanes: the stores are transposed across the warp
+              epi_apply_rows(p, m, img, n, r, in, lane);
+              continue;
+            }
+          }
+          if (!mvalid) continue;
           if (fused) {
             epi_apply<CH>(p, m, img, n, r, in);
             continue;
