@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
                                                    float* __restrict__ y, int ldy) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float xs[kGemvMaxM * kGemvMaxK];
+  __shared__ __align__(16) float xs[kGemvMaxM * kGemvMaxK];
   for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
     const float v = x[i];
     xs[i] = act_in ? silu_f(v) : v;
@@ -103,9 +103,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
 #pragma unroll
       for (int m = 0; m < kGemvMaxM; ++m) {
         if (m < M) {
-          const float* xr = xs + m * K + k0;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[r][m] += wf[e] * xr[e];
+          // two 16-byte shared loads per 8 weights (scalar loads here were the kernel's bottleneck:
+          // lanes 32 bytes apart, several-way bank conflicts per element)
+          const float4 xa = *reinterpret_cast<const float4*>(xs + m * K + k0);
+          const float4 xb = *reinterpret_cast<const float4*>(xs + m * K + k0 + 4);
+          acc[r][m] += wf[0] * xa.x + wf[1] * xa.y + wf[2] * xa.z + wf[3] * xa.w +
+                       wf[4] * xb.x + wf[5] * xb.y + wf[6] * xb.z + wf[7] * xb.w;
         }
       }
     }
