@@ -206,8 +206,9 @@ SDG_API int sdg_selftest_stalled_gemm(const uint16_t* x, const uint16_t* w, int 
 
 /* y = conv(x) (+bias[Co]) (+rowbias[b,Co]) (+residual) (act: 0 none, 1 SiLU).
  * x is [B,H,W,Ci1], x2 (optional, channel concat after x) [B,H,W,Ci2].
- * k = 3 (pad 1, stride 1 or 2) or 1. y is [B,Ho,Wo,Co]. For stride 2 the
- * caller supplies col_scratch of B*Ho*Wo*9*Ci fp16 (else NULL).
+ * k = 3 (pad 1, stride 1 or 2; stride 2 needs even H and W) or 1. y is
+ * [B,Ho,Wo,Co]. col_scratch is not used (kept for source compatibility; NULL
+ * is fine): stride 2 runs as an implicit GEMM too.
  * workspace (optional, fp32-aligned device memory): when the tile chooser
  * splits K across CTAs (small M, large K) it needs up to 32*M*Co*4 bytes; with
  * less (or NULL) the op runs without split-K. */

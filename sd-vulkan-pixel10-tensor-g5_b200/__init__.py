@@ -283,15 +283,14 @@ class Engine:
 # ------------------------------------------------------------------ op surface (torch CUDA tensors)
 def conv2d(x, w, bias, Co: int, k: int = 3, stride: int = 1, x2=None, rowbias=None, residual=None, act: int = 0,
            out=None, col_scratch=None, workspace=None, err_word=None, stream=None):
-    """x [B,H,W,Ci1] fp16 (x2 [B,H,W,Ci2] concatenated after it), w [Co][k*k][Ci] fp16."""
+    """x [B,H,W,Ci1] fp16 (x2 [B,H,W,Ci2] concatenated after it), w [Co][k*k][Ci] fp16.
+    col_scratch is accepted and ignored (stride 2 runs as an implicit GEMM)."""
     import torch
     B, H, W, Ci1 = x.shape
     Ci2 = 0 if x2 is None else x2.shape[3]
     Ho, Wo = (H, W) if stride == 1 else ((H - 1) // 2 + 1, (W - 1) // 2 + 1)
     if out is None:
         out = torch.empty((B, Ho, Wo, Co), dtype=torch.float16, device=x.device)
-    if stride == 2 and col_scratch is None:
-        col_scratch = torch.empty((B * Ho * Wo * 9 * (Ci1 + Ci2),), dtype=torch.float16, device=x.device)
     wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().sdg_conv2d(_ptr(x), _ptr(x2), B, H, W, Ci1, Ci2, _ptr(w), _ptr(bias), Co, k, stride, _ptr(rowbias),
                            _ptr(residual), act, _ptr(out), _ptr(col_scratch), _ptr(workspace), wsb, _ptr(err_word),

@@ -105,15 +105,14 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
   a.out = reinterpret_cast<__half*>(y);
   a.ws = static_cast<float*>(workspace);
   a.ws_bytes = workspace ? workspace_bytes : 0;
-  if (k == 3 && stride == 2) {
+  if (k == 3 && stride == 2) {  // implicit GEMM over the input walked with stride 2 (col_scratch unused)
     if (x2) return sdg::op_fail(SDG_ERR_SHAPE, "conv2d: stride 2 takes one source");
-    if (!col_scratch) return sdg::op_fail(SDG_ERR_ARG, "conv2d: stride 2 needs col_scratch");
-    const int Ho = (H - 1) / 2 + 1, Wo = (W - 1) / 2 + 1;
-    int st = cuda_status(sdg::launch_im2col3x3(reinterpret_cast<const __half*>(x), B, H, W, Ci, 2, 9 * Ci,
-                                               reinterpret_cast<__half*>(col_scratch), s), "im2col");
-    if (st) return st;
-    a.M = B * Ho * Wo; a.K = 9 * Ci; a.taps = 1;
-    a.a0 = reinterpret_cast<const __half*>(col_scratch); a.cin0 = 9 * Ci;
+    if (H % 2 || W % 2) return sdg::op_fail(SDG_ERR_SHAPE, "conv2d: stride 2 needs even H and W");
+    (void)col_scratch;
+    const int Ho = H / 2, Wo = W / 2;
+    a.M = B * Ho * Wo; a.K = 9 * Ci; a.taps = 9; a.stride = 2;
+    a.a0 = reinterpret_cast<const __half*>(x); a.cin0 = Ci;
+    a.B = B; a.H = H; a.W = W;
     a.rows_per_image = Ho * Wo;
     return cuda_status(sdg::launch_gemm(a, err, s), "conv2d");
   }

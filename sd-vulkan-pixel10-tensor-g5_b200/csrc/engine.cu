@@ -791,22 +791,15 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
 }
 
 Buf Builder::downsample(const ConvW& c, const Buf& x, int H, int W) {
+  // 3x3 stride-2 pad-1 convolution as an implicit GEMM: the tensor map walks the input with element
+  // stride 2 (vk_engine.cpp:689-692 runs it as im2col + matmul)
   const int B = pl_.B, Ho = H / 2, Wo = W / 2, M = B * Ho * Wo;
   Buf out{alloc_h((size_t)M * c.Co), c.Co};
-  const size_t mark = off_;
-  __half* col = alloc_h((size_t)M * 9 * x.C);
-  if (!dry_ && ok()) {
-    issue(kCatMisc, "im2col", 1, [=, xp = x.p, C = x.C](cudaStream_t s) {
-      return launch_im2col3x3(xp, B, H, W, C, 2, 9 * C, col, s);
-    });
-  } else {
-    launches_++;
-  }
   GemmArgs a;
-  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.a0 = col; a.cin0 = 9 * x.C; set_w(a, c.w, c.w8, c.ws); a.bias = c.b;
-  a.out = out.p;
-  gemm(a, kCatGemm);
-  off_ = mark;
+  a.M = M; a.N = c.Co; a.K = 9 * x.C; a.taps = 9; a.stride = 2; a.a0 = x.p; a.cin0 = x.C; a.B = B; a.H = H; a.W = W;
+  a.rows_per_image = Ho * Wo;
+  set_w(a, c.w, c.w8, c.ws); a.bias = c.b; a.out = out.p;
+  gemm(a, kCatConv3);
   return out;
 }
 

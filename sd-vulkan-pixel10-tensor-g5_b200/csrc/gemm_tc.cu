@@ -48,7 +48,8 @@ constexpr uint32_t kATileBytes = BM * BK * 2;  // 16 KB
 struct GemmDev {
   int M, N, K;
   int taps, cin0, cin1;
-  int H, W;                // conv geometry
+  int H, W;                // conv geometry (input image)
+  int cs;                  // conv stride (1 or 2): output Ho = H / cs, Wo = W / cs
   int epi, act;
   const float* bias;
   const float* rowbias;
@@ -482,10 +483,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
         const int m0 = m_blk * TM + (int)rank * BM;          // this CTA's A rows
         const int n0 = n_blk * BN + (int)rank * C::kBRows;   // this CTA's W rows
         int img0 = 0, y0 = 0;
-        if (p.taps == 9) {
-          const int hw = p.H * p.W;
-          img0 = m0 / hw;
-          y0 = (m0 % hw) / p.W;
+        if (p.taps == 9) {  // output geometry; the tensor map walks the input with stride cs
+          const int wo = p.W / p.cs, hwo = (p.H / p.cs) * wo;
+          img0 = m0 / hwo;
+          y0 = (m0 % hwo) / wo;
         }
         for (int kb = kb0; kb < kb1; kb += G, ++it) {
           const int s = it % S;
@@ -512,7 +513,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
             if constexpr (PAIR) {
               if (p.taps == 9) {
                 const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-                tma_load_4d_pair(dA, ma, fb, ch, dx, y0 + dy, img0);
+                tma_load_4d_pair(dA, ma, fb, ch, dx, p.cs * y0 + dy, img0);
               } else {
                 tma_load_2d_pair(dA, ma, fb, ch, m0);
               }
@@ -520,7 +521,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
             } else {
               if (p.taps == 9) {
                 const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-                tma_load_4d(dA, ma, fb, ch, dx, y0 + dy, img0);
+                tma_load_4d(dA, ma, fb, ch, dx, p.cs * y0 + dy, img0);
               } else {
                 tma_load_2d(dA, ma, fb, ch, m0);
               }
@@ -1056,7 +1057,7 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   GemmDev d{};
   d.M = a.M; d.N = a.N; d.K = a.K;
   d.taps = a.taps; d.cin0 = a.cin0; d.cin1 = a.cin1;
-  d.H = a.H; d.W = a.W;
+  d.H = a.H; d.W = a.W; d.cs = a.taps == 9 ? a.stride : 1;
   d.epi = a.epi; d.act = a.act;
   d.bias = a.bias; d.rowbias = a.rowbias; d.rowbias_ld = a.rowbias_ld;
   d.rows_per_image = a.rows_per_image > 0 ? a.rows_per_image : 1;
@@ -1079,23 +1080,29 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
 
   CUtensorMap ma0{}, ma1{}, mw{};
   if (a.taps == 9) {
-    const int hw = a.H * a.W;
+    // Box over the input {64 channels, row, rows, images}, shifted per tap; with stride 2 the box spans
+    // twice the output extent in x and y and TMA loads every second element (element strides 2), so
+    // the tile still lands as 128 output pixels x 64 channels. Out-of-range rows / columns read zero.
+    const int st = a.stride;
+    if (!(st == 1 || st == 2) || a.H % st || a.W % st) return cudaErrorInvalidValue;
+    const int ho = a.H / st, wo = a.W / st, hw = a.H * a.W, hwo = ho * wo;
     int box_h, box_b;
-    if (a.W > 128 || (BM % a.W) != 0) return cudaErrorInvalidValue;
-    if (hw >= BM) {
-      box_h = BM / a.W; box_b = 1;
-      if (a.H % box_h) return cudaErrorInvalidValue;
+    if (wo > 128 || (BM % wo) != 0) return cudaErrorInvalidValue;
+    if (hwo >= BM) {
+      box_h = BM / wo; box_b = 1;
+      if (ho % box_h) return cudaErrorInvalidValue;
     } else {
-      if (BM % hw) return cudaErrorInvalidValue;
-      box_h = a.H; box_b = BM / hw;
+      if (BM % hwo) return cudaErrorInvalidValue;
+      box_h = ho; box_b = BM / hwo;
     }
     auto mk4 = [&](CUtensorMap* m, const __half* base, int c) {
       uint64_t dims[4] = {(uint64_t)c, (uint64_t)a.W, (uint64_t)a.H, (uint64_t)a.B};
       uint64_t str[3] = {(uint64_t)c * 2, (uint64_t)a.W * c * 2, (uint64_t)hw * c * 2};
-      uint32_t box[4] = {BK, (uint32_t)a.W, (uint32_t)box_h, (uint32_t)box_b};
-      return make_tmap(m, base, 4, dims, str, box);
+      uint32_t box[4] = {BK, (uint32_t)(st * wo), (uint32_t)(st * box_h), (uint32_t)box_b};
+      const uint32_t estr[4] = {1u, (uint32_t)st, (uint32_t)st, 1u};
+      return make_tmap(m, base, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, estr);
     };
-    if (a.M != a.B * hw) return cudaErrorInvalidValue;
+    if (a.M != a.B * hwo) return cudaErrorInvalidValue;
     if (!mk4(&ma0, a.a0, a.cin0)) return cudaErrorInvalidValue;
     if (a.cin1 > 0 && !mk4(&ma1, a.a1, a.cin1)) return cudaErrorInvalidValue;
   } else {

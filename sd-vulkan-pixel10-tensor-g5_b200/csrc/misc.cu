@@ -1,7 +1,7 @@
 // misc.cu — small bandwidth kernels around the tensor-core path:
 // time embedding (VulkanUnetPipeline.kt:36-46 sinusoid, computed in fp64),
 // small-M GEMV (time MLP vk_engine.cpp:716-717, per-ResNet time_emb_proj
-// :627-630, batched into one launch), im2col for the stride-2 downsample and
+// :627-630, batched into one launch), im2col for
 // the 4-channel conv_in, nearest 2x upsample (upsample_f32.comp), channel
 // concat (vk_engine.cpp:677-688), add, and the fused CFG-combine + LCM step
 // (VulkanUnetPipeline.kt:86, LcmScheduler.kt:56-82).
@@ -130,29 +130,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(const float* __restrict__ x, 
   }
 }
 
-// col[(b*Ho+oy)*Wo+ox, tap*C + c] = x[b, oy*s+ky-1, ox*s+kx-1, c] (0 outside)
-__global__ void im2col3x3_kernel(const __half* __restrict__ x, int B, int H, int W, int C, int stride, int Ho, int Wo,
-                                 int Kpad, __half* __restrict__ col) {
-  pdl_wait();
-  pdl_trigger();
-  const int nvec = C / 8;
-  const size_t total = (size_t)B * Ho * Wo * 9 * nvec;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int v = (int)(i % nvec);
-    const size_t r = i / nvec;
-    const int tap = (int)(r % 9);
-    const size_t pix = r / 9;
-    const int ox = (int)(pix % Wo);
-    const int oy = (int)((pix / Wo) % Ho);
-    const int b = (int)(pix / ((size_t)Wo * Ho));
-    const int iy = oy * stride + tap / 3 - 1, ix = ox * stride + tap % 3 - 1;
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (iy >= 0 && iy < H && ix >= 0 && ix < W) u = *reinterpret_cast<const uint4*>(x + (((size_t)b * H + iy) * W + ix) * C + v * 8);
-    *reinterpret_cast<uint4*>(col + pix * Kpad + tap * C + v * 8) = u;
-  }
-}
-
-// conv_in operand: lat NCHW fp32 [B,Cl,H,W] -> col [B*H*W, Kpad], K index = tap*Cl + c, zero padded.
 __global__ void latent_im2col_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W, int Kpad,
                                      __half* __restrict__ col) {
   pdl_wait();
@@ -287,15 +264,6 @@ cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
-}
-
-cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int stride, int Kpad, __half* col,
-                             cudaStream_t s) {
-  if (C % 8 || Kpad < 9 * C) return cudaErrorInvalidValue;
-  const int Ho = (H + 2 - 3) / stride + 1, Wo = (W + 2 - 3) / stride + 1;
-  const size_t total = (size_t)B * Ho * Wo * 9 * (C / 8);
-  return launch_kernel(im2col3x3_kernel, dim3(grid_for(total)), dim3(256), 0, s, 0, x, B, H, W, C, stride, Ho, Wo, Kpad,
-                       col);
 }
 
 cudaError_t launch_latent_im2col(const float* lat, int B, int Cl, int H, int W, int Kpad, __half* col, cudaStream_t s) {

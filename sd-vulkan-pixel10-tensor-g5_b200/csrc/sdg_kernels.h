@@ -18,7 +18,7 @@ enum EpiMode : int {
 // One GEMM / implicit-GEMM convolution: D[M,N] = A[M,K] * W[N,K]^T with the
 // fused epilogue  act(D + bias[n] + rowbias[img(m), n] + residual[m, n]).
 // A is either a row-major [M, K] activation matrix (taps == 1) or, for a
-// stride-1 pad-1 3x3 convolution (taps == 9), gathered on the fly from the
+// pad-1 3x3 convolution of stride 1 or 2 (taps == 9), gathered on the fly from the
 // NHWC input by 4D TMA boxes shifted per tap (out-of-range rows/columns read
 // as zero == the convolution's zero padding). A may come from two sources
 // (channel concat [src0 ; src1]): K-chunks with channel < cin0 read src0.
@@ -29,7 +29,8 @@ struct GemmArgs {
   const __half* a1 = nullptr;  // source 1 (concat) or null
   int cin0 = 0, cin1 = 0;      // channels per tap from each source
   int lda0 = 0, lda1 = 0;      // row strides (elements) for taps == 1 (default cin)
-  int B = 1, H = 1, W = 1;     // conv geometry (taps == 9)
+  int B = 1, H = 1, W = 1;     // conv geometry (taps == 9): the INPUT image
+  int stride = 1;              // taps == 9: 1, or 2 (output H/2 x W/2, pad 1; M = B * H/2 * W/2)
   const __half* w = nullptr;   // [N, K] K-major (conv: [Co][tap][Cin])
   const int8_t* w8 = nullptr;  // weight-only int8 alternative to w: [N, K] ...
   const float* wscale = nullptr;  // ... with per-row (output channel) scale [N]
@@ -106,8 +107,6 @@ cudaError_t launch_time_embedding(const float* timesteps, int n_t, int B, const 
 // either fp16 w [N,K], or int8 w8 [N,K] with per-row scale ws [N] (exactly one of w / w8).
 cudaError_t launch_gemv(const float* x, int M, int K, const __half* w, const int8_t* w8, const float* ws,
                         const float* bias, int N, int act_in, int act_out, float* y, int ldy, cudaStream_t s);
-cudaError_t launch_im2col3x3(const __half* x, int B, int H, int W, int C, int stride, int Kpad, __half* col,
-                             cudaStream_t s);
 cudaError_t launch_latent_im2col(const float* lat_nchw, int B, int C, int H, int W, int Kpad, __half* col,
                                  cudaStream_t s);
 cudaError_t launch_upsample2x(const __half* x, int B, int H, int W, int C, __half* y, cudaStream_t s);

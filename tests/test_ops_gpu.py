@@ -149,9 +149,9 @@ def test_conv1x1_concat(sdg, cuda, gen):
     assert rel(nchw(y), F.conv2d(torch.cat([x1, x2], 1).float(), w.float(), b)) < TOL
 
 
-@pytest.mark.parametrize("C,H", [(320, 64), (640, 32), (1280, 16)])
-def test_conv3x3_stride2(sdg, cuda, gen, C, H):
-    B = 2
+@pytest.mark.parametrize("B,C,H", [(2, 320, 64), (2, 640, 32), (2, 1280, 16),   # the three downsamplers
+                                   (1, 1280, 16), (3, 640, 16), (1, 320, 8)])   # partial tiles, images per tile
+def test_conv3x3_stride2(sdg, cuda, gen, B, C, H):
     x = rnd(B, C, H, H, g=gen).half()
     w = rnd(C, C, 3, 3, std=1 / math.sqrt(9 * C), g=gen).half()
     b = rnd(C, std=0.1, g=gen).float()
