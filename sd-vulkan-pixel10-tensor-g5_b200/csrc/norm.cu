@@ -3,7 +3,8 @@
 // GroupNorm replaces groupnorm_f32.comp / groupnorm_silu.comp
 // (vk_engine.cpp:548-549): statistics per (image, group), y = (x-mu)*rstd*g+b,
 // optional SiLU. The reference reduces one group per workgroup with
-// var = E[x^2] - mu^2 (groupnorm_f32.comp:24-25). Here:
+// var = E[x^2] - mu^2 (groupnorm_f32.comp:24-25). Here one launch
+// (gn_fused_kernel, below) for every shape the UNet has; otherwise two:
 //   kernel 1 (stats): one block per (group, image), exact two-pass mean and
 //                     centred variance over the group's elements read
 //                     straight from L2 (the producer just wrote them), fixed
@@ -140,34 +141,44 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
 }
 
 // Fused single-launch GroupNorm: a cluster of K CTAs (K = 1..16, chosen per
-// launch from the work: ~40 KB of input per CTA) per (channel slice, image).
-// Each CTA owns 1/K of the image's pixels for a slice of whole groups. Every
-// thread issues all loads of its share of the chunk up front (at most kGnMaxV
-// 16-byte vectors, kept in registers: high memory-level parallelism, one
-// global read per element). Each CTA reduces its own chunk exactly (two
-// passes: mean, then centred sum of squares, both over registers); the K
-// per-CTA (mean, M2) pairs are exchanged once through distributed shared
-// memory and merged in rank order with the pairwise update of Chan, Golub and
-// LeVeque (deterministic). A third pass normalises from registers. Rank 0
+// launch from the work: ~20 KB of input per CTA) per (channel slice, image).
+// Each CTA owns 1/K of the image's pixels for a slice of whole groups; every
+// thread owns one 8-channel vector column of it (at most kGnMaxV pixels, all
+// loads issued up front and kept in registers: one global read per element).
+// The affine parameters do not depend on the previous kernel and are fetched
+// before its completion (pdl_wait).
+// Statistics in one pass over the registers, as sums of shifted values: every
+// group is shifted by one of its own elements (the image's pixel-0 value of
+// the group's first channel, the same in every CTA of the cluster), so
+// var = S2/n - (S1/n)^2 stays well conditioned whatever the group's mean
+// (the shifted-data variance of Chan, Golub and LeVeque). A thread's vector
+// spans at most two groups (>= 8 channels per group); its two (S1, S2) pairs
+// go through shared memory to one warp per group, which sums them in a fixed
+// order and pushes the CTA's pair into slot [rank] of every cluster CTA
+// (st.shared::cluster). After one cluster barrier each CTA adds the K slots in
+// rank order (deterministic, no atomics) and normalises from registers. Rank 0
 // also records (mean, rstd) per group.
 // Clusters of up to 8 CTAs (the portable size) where the shape allows: a
-// 16-CTA cluster needs 16 free SMs inside one GPC, and at one 512-thread CTA
-// per SM only 7 such clusters fit on a B200 at once. 16 (non-portable, opted
-// in at launch) only for shapes no smaller cluster can hold.
+// 16-CTA cluster needs 16 free SMs inside one GPC. 16 (non-portable, opted in
+// at launch) only for shapes no smaller cluster can hold.
 constexpr int kGnMaxCluster = 16;
 constexpr int kGnPreferredCluster = 8;
 constexpr int kGnFusedThreads = 256;  // two CTAs per SM
 constexpr int kGnMaxV = 16;
 
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kGnFusedThreads, 2)
     gn_fused_kernel(GroupNormArgs a, int nslices, float2* __restrict__ gstat) {
-  pdl_wait();
-  pdl_trigger();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
+  // first cluster barrier phase: every CTA of the cluster has started before any CTA stores into its
+  // shared memory (the matching wait comes just before the push)
+  cluster_arrive_relaxed();
   const int rank = (int)cluster.block_rank();
   const int kc = (int)cluster.num_blocks();
   const int slice = blockIdx.x / kc;
@@ -182,20 +193,26 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
   const int chunk = (a.HW + kc - 1) / kc;
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
-  __shared__ float red[kGnFusedThreads * 8];  // [rows][Ws] per-channel partials (rows * Ws <= threads * 8)
-  __shared__ float red2[kGnFusedThreads];  // [row slice][Ws] (slices * Ws <= threads)
-  __shared__ float chan[320];        // per-channel CTA sums
-  __shared__ float gsum[32];         // per-group CTA sums
-  __shared__ float2 part[32];        // this CTA's (mean, M2) per group, read by the whole cluster
-  __shared__ float2 allp[kGnMaxCluster][32];
+  __shared__ float2 pa[kGnFusedThreads], pb[kGnFusedThreads];  // per thread: (S1, S2) of its first / second group
+  __shared__ float2 allp[kGnMaxCluster][32];                   // [source rank][group], pushed by the cluster
   __shared__ float gmu[32], grs[32];
-  __shared__ float sc[320], sh[320];
   const int t = threadIdx.x;
   const int v = t % nv, r = t / nv;
   const bool active = r < rows;
-  const int c0 = cbeg + v * 8;       // first channel of this thread's vector
+  const int cl0 = v * 8;             // slice-local first channel of this thread's vector
+  const int c0 = cbeg + cl0;
+  const int ga = cl0 / cpg;          // slice-local group of channels [0, split) of the vector ...
+  const int split = min(8, (ga + 1) * cpg - cl0);  // ... the rest belong to group ga + 1
   const int cnt = (active && p0 + r < p1) ? (p1 - p0 - r + rows - 1) / rows : 0;
-  const float n_loc = (float)max(0, p1 - p0) * cpg;
+
+  float gam[8], bet[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    gam[e] = active ? a.gamma[c0 + e] : 0.f;
+    bet[e] = active ? a.beta[c0 + e] : 0.f;
+  }
+  pdl_wait();
+  pdl_trigger();
 
   uint4 xs[kGnMaxV];
   int cl;
@@ -204,6 +221,15 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
 #pragma unroll
   for (int i = 0; i < kGnMaxV; ++i)
     if (i < cnt) xs[i] = *reinterpret_cast<const uint4*>(src0 + cl + i * pstride);
+  // the shift of slice-local group gl: pixel 0 of the image, the group's first channel
+  auto shift_of = [&](int gl) -> float {
+    int c;
+    const __half* p = gn_src(a, cbeg + gl * cpg, img_base, c);
+    return __half2float(p[c]);
+  };
+  const float ka = active ? shift_of(ga) : 0.f;
+  const float kb = (active && split < 8) ? shift_of(ga + 1) : ka;
+  const float kown = t < gps ? shift_of(t) : 0.f;  // merge thread of group t
 
   auto unpack = [](const uint4& u, float (&x)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
@@ -214,58 +240,14 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
       x[2 * e + 1] = f.y;
     }
   };
-  // per-thread channel partials -> per-group CTA sums in gsum (fixed order)
-  auto cta_group_sums = [&](const float (&acc)[8]) {
-    if (active) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) red[r * Ws + v * 8 + e] = acc[e];
-    }
-    __syncthreads();
-    const int nslc = kGnFusedThreads / Ws;
-    if (t < nslc * Ws) {
-      const int c = t % Ws, rs = t / Ws;
-      float s = 0.f;
-      for (int rr = rs; rr < rows; rr += nslc) s += red[rr * Ws + c];
-      red2[rs * Ws + c] = s;
-    }
-    __syncthreads();
-    if (t < Ws) {
-      float s = 0.f;
-      for (int rs = 0; rs < nslc; ++rs) s += red2[rs * Ws + t];
-      chan[t] = s;
-    }
-    __syncthreads();
-    for (int g = t >> 5; g < gps; g += kGnFusedThreads / 32) {
-      float s = 0.f;
-      for (int j = (t & 31); j < cpg; j += 32) s += chan[g * cpg + j];
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if ((t & 31) == 0) gsum[g] = s;
-    }
-    __syncthreads();
-  };
-
-  // pass 1: this CTA's group means
-  float acc[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll
-  for (int i = 0; i < kGnMaxV; ++i) {
-    if (i < cnt) {
-      float x[8];
-      unpack(xs[i], x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += x[e];
-    }
-  }
-  cta_group_sums(acc);
-  float mu[8];
+  // one pass: per-channel sums of shifted values and of their squares
+  float s1[8], s2[8], kk[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    acc[e] = 0.f;
-    mu[e] = (active && n_loc > 0.f) ? gsum[(v * 8 + e) / cpg] / n_loc : 0.f;
+    s1[e] = 0.f;
+    s2[e] = 0.f;
+    kk[e] = e < split ? ka : kb;
   }
-  if (t < gps) part[t].x = n_loc > 0.f ? gsum[t] / n_loc : 0.f;
-  // pass 2: centred sums of squares about this CTA's means
 #pragma unroll
   for (int i = 0; i < kGnMaxV; ++i) {
     if (i < cnt) {
@@ -273,51 +255,76 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
       unpack(xs[i], x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float d = x[e] - mu[e];
-        acc[e] += d * d;
+        const float d = x[e] - kk[e];
+        s1[e] += d;
+        s2[e] = fmaf(d, d, s2[e]);
       }
     }
   }
-  cta_group_sums(acc);
-  if (t < gps) part[t].y = gsum[t];
-  // one exchange: every CTA gathers all K (mean, M2) pairs, then merges them in rank order
-  cluster_arrive();
-  cluster_wait();
-  for (int i = t; i < kc * gps; i += kGnFusedThreads) {
-    const int q = i / gps, g = i - q * gps;
-    allp[q][g] = cluster.map_shared_rank(&part[0], q)[g];
-  }
-  cluster_arrive();  // this CTA no longer reads remote memory; the matching wait is at the end
-  __syncthreads();
-  if (t < gps) {
-    float n = 0.f, m = 0.f, m2 = 0.f;
-    for (int q = 0; q < kc; ++q) {
-      const int q0 = q * chunk, q1 = min(a.HW, q0 + chunk);
-      const float nb = (float)max(0, q1 - q0) * cpg;
-      if (nb <= 0.f) continue;
-      const float2 pb = allp[q][t];
-      const float nn = n + nb;
-      const float d = pb.x - m;
-      m += d * (nb / nn);
-      m2 += pb.y + d * d * (n * nb / nn);
-      n = nn;
+  float2 qa = make_float2(0.f, 0.f), qb = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if (e < split) {
+      qa.x += s1[e];
+      qa.y += s2[e];
+    } else {
+      qb.x += s1[e];
+      qb.y += s2[e];
     }
-    gmu[t] = m;
-    grs[t] = rsqrtf(m2 / n + a.eps);
+  }
+  pa[t] = qa;
+  pb[t] = qb;
+  __syncthreads();
+  cluster_wait();  // first phase: the whole cluster is running
+  // one warp per group: the group's vector columns, rows in a fixed order, then a butterfly (every lane
+  // ends with the same sum); the CTA's pair is pushed to slot [rank] of every CTA of the cluster
+  const int w = t >> 5, lane = t & 31;
+  for (int g = w; g < gps; g += kGnFusedThreads / 32) {
+    const int vlo = (g * cpg) / 8, vhi = ((g + 1) * cpg - 1) / 8;
+    float S1 = 0.f, S2 = 0.f;
+    for (int vv = vlo; vv <= vhi; ++vv) {
+      const float2* src = (vv * 8) / cpg == g ? pa : pb;  // the vector starts in g, or in g - 1
+      for (int rr = lane; rr < rows; rr += 32) {
+        const float2 q = src[rr * nv + vv];
+        S1 += q.x;
+        S2 += q.y;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      S1 += __shfl_xor_sync(0xffffffffu, S1, o);
+      S2 += __shfl_xor_sync(0xffffffffu, S2, o);
+    }
+    if (lane < kc) *cluster.map_shared_rank(&allp[rank][g], lane) = make_float2(S1, S2);
+  }
+  cluster_arrive();  // second phase: the pushes are visible to their targets after the wait
+  cluster_wait();
+  if (t < gps) {
+    float S1 = 0.f, S2 = 0.f;
+    for (int q = 0; q < kc; ++q) {
+      S1 += allp[q][t].x;
+      S2 += allp[q][t].y;
+    }
+    const float n = (float)a.HW * cpg;
+    const float m1 = S1 / n;
+    const float var = fmaxf(S2 / n - m1 * m1, 0.f);
+    const float mu = kown + m1;
+    const float rs = rsqrtf(var + a.eps);
+    gmu[t] = mu;
+    grs[t] = rs;
+    if (rank == 0 && gstat) gstat[img * a.groups + slice * gps + t] = make_float2(mu, rs);
   }
   __syncthreads();
-  if (rank == 0 && t < gps && gstat) gstat[img * a.groups + slice * gps + t] = make_float2(gmu[t], grs[t]);
-  for (int c = t; c < Ws; c += blockDim.x) {
-    const int g = c / cpg;
-    const float s = grs[g] * a.gamma[cbeg + c];
-    sc[c] = s;
-    sh[c] = a.beta[cbeg + c] - gmu[g] * s;
-  }
-  __syncthreads();
-  if (active) {
+  if (cnt > 0) {
+    const int gb = split < 8 ? ga + 1 : ga;
+    const float mua = gmu[ga], rsa = grs[ga], mub = gmu[gb], rsb = grs[gb];
     float scl[8], shf[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) { scl[e] = sc[v * 8 + e]; shf[e] = sh[v * 8 + e]; }
+    for (int e = 0; e < 8; ++e) {
+      const float m = e < split ? mua : mub;
+      scl[e] = (e < split ? rsa : rsb) * gam[e];
+      shf[e] = bet[e] - m * scl[e];
+    }
     __half* dst0 = a.y + (img_base + p0 + r) * C + c0;
 #pragma unroll
     for (int i = 0; i < kGnMaxV; ++i) {
@@ -328,8 +335,8 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
         uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float y0 = x[2 * e] * scl[2 * e] + shf[2 * e];
-          float y1 = x[2 * e + 1] * scl[2 * e + 1] + shf[2 * e + 1];
+          float y0 = fmaf(x[2 * e], scl[2 * e], shf[2 * e]);
+          float y1 = fmaf(x[2 * e + 1], scl[2 * e + 1], shf[2 * e + 1]);
           if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
           ow[e] = pack_half2(y0, y1);
         }
@@ -337,7 +344,6 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
       }
     }
   }
-  cluster_wait();  // no CTA leaves while another may still read its `part`
 }
 
 // Cluster size for a (slice, image): ~20 KB of input per CTA, at most `maxc`,
@@ -356,14 +362,15 @@ int gn_cluster_ctas(int HW, int Ws, int maxc = kGnPreferredCluster) {
 // Slice count (dividing the group count; whole groups and whole 8-channel
 // vectors per slice) for the fused kernel: the one giving the most CTAs per
 // image up to ~72 (so a batch of 2 stays within one wave of 148 SMs), among
-// slices of at least 40 channels when any fits; 0 if none fits.
+// slices of at least 40 channels when any fits; 0 if none fits or a group has
+// fewer than 8 channels (an 8-channel vector would span more than two groups).
 int gn_fused_slices(int C, int groups, int HW, int maxc = kGnPreferredCluster) {
   int best = 0, best_ctas = 0;
   bool best_wide = false;
   for (int ns = 1; ns <= groups; ns *= 2) {
     if (groups % ns || C % ns) continue;
     const int Ws = C / ns;
-    if (Ws % 8 || Ws > 256 || (Ws % (C / groups)) || Ws / (C / groups) > 32) continue;
+    if (Ws % 8 || Ws > 256 || (Ws % (C / groups)) || Ws / (C / groups) > 32 || C / groups < 8) continue;
     const int k = gn_cluster_ctas(HW, Ws, maxc);
     if (k == 0) continue;
     const int ctas = ns * k;

@@ -176,6 +176,22 @@ def test_groupnorm(sdg, cuda, gen, B, C, H, silu, eps, shift):
     assert rel(nchw(y.reshape(B, H, H, C)), ref) < TOL
 
 
+@pytest.mark.parametrize("C,H", [(320, 64), (1280, 8)])
+def test_groupnorm_offset_data_outlier_shift(sdg, cuda, gen, C, H):
+    # the fused kernel sums values shifted by each group's pixel-0 element: a mean 40x the spread,
+    # with pixel 0 a further 50 spreads away, still gives the two-pass result
+    B = 2
+    x = rnd(B, C, H, H, g=gen) * 0.5 + 20.0
+    x[:, :, 0, 0] += 25.0
+    x = x.half()
+    gam = rnd(C, std=0.3, g=gen).float() + 1.0
+    bet = rnd(C, std=0.3, g=gen).float()
+    y = sdg.groupnorm(nhwc(x).reshape(B, H * H, C), gam, bet, 1e-5, True)
+    torch.cuda.synchronize()
+    ref = R.groupnorm(x.float(), gam, bet, 1e-5, True)
+    assert rel(nchw(y.reshape(B, H, H, C)), ref) < TOL
+
+
 def test_groupnorm_concat_straddling_groups(sdg, cuda, gen):
     # up_blocks.1.resnets.2: concat 1280 + 640 -> 1920 channels, 60 per group: groups straddle the sources
     B, C1, C2, H = 2, 1280, 640, 16
