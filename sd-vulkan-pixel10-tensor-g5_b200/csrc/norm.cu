@@ -156,8 +156,9 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(GroupNormArgs a, i
 // go through shared memory to one warp per group, which sums them in a fixed
 // order and pushes the CTA's pair into slot [rank] of every cluster CTA
 // (st.shared::cluster). After one cluster barrier each CTA adds the K slots in
-// rank order (deterministic, no atomics) and normalises from registers. Rank 0
-// also records (mean, rstd) per group.
+// rank order (deterministic, no atomics) and normalises from registers (fp32
+// pairs in f32x2 instructions, rounded to fp16, SiLU on the f16x2 pair: one
+// tanh.approx.f16x2 per two values). Rank 0 also records (mean, rstd) per group.
 // Clusters of up to 8 CTAs (the portable size) where the shape allows: a
 // 16-CTA cluster needs 16 free SMs inside one GPC. 16 (non-portable, opted in
 // at launch) only for shapes no smaller cluster can hold.
@@ -193,7 +194,8 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
   const int chunk = (a.HW + kc - 1) / kc;
   const int p0 = rank * chunk, p1 = min(a.HW, p0 + chunk);
   const size_t img_base = (size_t)img * a.HW;
-  __shared__ float2 pa[kGnFusedThreads], pb[kGnFusedThreads];  // per thread: (S1, S2) of its first / second group
+  // per thread (r, v), at [v * rows + r]: (S1, S2) of its first / second group
+  __shared__ float2 pa[kGnFusedThreads], pb[kGnFusedThreads];
   __shared__ float2 allp[kGnMaxCluster][32];                   // [source rank][group], pushed by the cluster
   __shared__ float gmu[32], grs[32];
   const int t = threadIdx.x;
@@ -204,6 +206,7 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
   const int ga = cl0 / cpg;          // slice-local group of channels [0, split) of the vector ...
   const int split = min(8, (ga + 1) * cpg - cl0);  // ... the rest belong to group ga + 1
   const int cnt = (active && p0 + r < p1) ? (p1 - p0 - r + rows - 1) / rows : 0;
+  const float inv_n = 1.f / ((float)a.HW * cpg);
 
   float gam[8], bet[8];
 #pragma unroll
@@ -231,64 +234,57 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
   const float kb = (active && split < 8) ? shift_of(ga + 1) : ka;
   const float kown = t < gps ? shift_of(t) : 0.f;  // merge thread of group t
 
-  auto unpack = [](const uint4& u, float (&x)[8]) {
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
+  // one pass: per-channel sums of shifted values and of their squares (channel pairs in f32x2)
+  float2 s1[4], s2[4], kk[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float2 f = __half22float2(h[e]);
-      x[2 * e] = f.x;
-      x[2 * e + 1] = f.y;
-    }
-  };
-  // one pass: per-channel sums of shifted values and of their squares
-  float s1[8], s2[8], kk[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    s1[e] = 0.f;
-    s2[e] = 0.f;
-    kk[e] = e < split ? ka : kb;
+  for (int j = 0; j < 4; ++j) {
+    s1[j] = make_float2(0.f, 0.f);
+    s2[j] = make_float2(0.f, 0.f);
+    kk[j] = make_float2(2 * j < split ? ka : kb, 2 * j + 1 < split ? ka : kb);
   }
 #pragma unroll
   for (int i = 0; i < kGnMaxV; ++i) {
     if (i < cnt) {
-      float x[8];
-      unpack(xs[i], x);
+      const __half2* h = reinterpret_cast<const __half2*>(&xs[i]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float d = x[e] - kk[e];
-        s1[e] += d;
-        s2[e] = fmaf(d, d, s2[e]);
+      for (int j = 0; j < 4; ++j) {
+        const float2 d = sub_f32x2(__half22float2(h[j]), kk[j]);
+        s1[j] = add_f32x2(s1[j], d);
+        s2[j] = fma_f32x2(d, d, s2[j]);
       }
     }
   }
   float2 qa = make_float2(0.f, 0.f), qb = make_float2(0.f, 0.f);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
+    const float a1 = (e & 1) ? s1[e >> 1].y : s1[e >> 1].x, a2 = (e & 1) ? s2[e >> 1].y : s2[e >> 1].x;
     if (e < split) {
-      qa.x += s1[e];
-      qa.y += s2[e];
+      qa.x += a1;
+      qa.y += a2;
     } else {
-      qb.x += s1[e];
-      qb.y += s2[e];
+      qb.x += a1;
+      qb.y += a2;
     }
   }
-  pa[t] = qa;
-  pb[t] = qb;
+  if (active) {
+    pa[v * rows + r] = qa;
+    pb[v * rows + r] = qb;
+  }
   __syncthreads();
   cluster_wait();  // first phase: the whole cluster is running
-  // one warp per group: the group's vector columns, rows in a fixed order, then a butterfly (every lane
-  // ends with the same sum); the CTA's pair is pushed to slot [rank] of every CTA of the cluster
+  // one warp per group: the group's vector columns [vlo, vhi] (contiguous in pa / pb), strided over
+  // the lanes in a fixed order, then a butterfly (every lane ends with the same sum); the CTA's pair is
+  // pushed to slot [rank] of every CTA of the cluster. Only column vlo can start in group g - 1 (its
+  // second-group sums, pb, belong to g).
   const int w = t >> 5, lane = t & 31;
   for (int g = w; g < gps; g += kGnFusedThreads / 32) {
-    const int vlo = (g * cpg) / 8, vhi = ((g + 1) * cpg - 1) / 8;
+    const int vlo = (g * cpg) >> 3, vhi = ((g + 1) * cpg - 1) >> 3;
+    const int b_end = vlo * 8 < g * cpg ? (vlo + 1) * rows : vlo * rows;
     float S1 = 0.f, S2 = 0.f;
-    for (int vv = vlo; vv <= vhi; ++vv) {
-      const float2* src = (vv * 8) / cpg == g ? pa : pb;  // the vector starts in g, or in g - 1
-      for (int rr = lane; rr < rows; rr += 32) {
-        const float2 q = src[rr * nv + vv];
-        S1 += q.x;
-        S2 += q.y;
-      }
+    for (int i = vlo * rows + lane; i < (vhi + 1) * rows; i += 32) {
+      const float2 q = i < b_end ? pb[i] : pa[i];
+      S1 += q.x;
+      S2 += q.y;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -305,9 +301,8 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
       S1 += allp[q][t].x;
       S2 += allp[q][t].y;
     }
-    const float n = (float)a.HW * cpg;
-    const float m1 = S1 / n;
-    const float var = fmaxf(S2 / n - m1 * m1, 0.f);
+    const float m1 = S1 * inv_n;
+    const float var = fmaxf(S2 * inv_n - m1 * m1, 0.f);
     const float mu = kown + m1;
     const float rs = rsqrtf(var + a.eps);
     gmu[t] = mu;
@@ -325,20 +320,25 @@ __global__ void __launch_bounds__(kGnFusedThreads, 2)
       scl[e] = (e < split ? rsa : rsb) * gam[e];
       shf[e] = bet[e] - m * scl[e];
     }
+    float2 scl2[4], shf2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      scl2[j] = make_float2(scl[2 * j], scl[2 * j + 1]);
+      shf2[j] = make_float2(shf[2 * j], shf[2 * j + 1]);
+    }
     __half* dst0 = a.y + (img_base + p0 + r) * C + c0;
+    // normalise in fp32 (f32x2), round to fp16, SiLU on the f16x2 pair
 #pragma unroll
     for (int i = 0; i < kGnMaxV; ++i) {
       if (i < cnt) {
-        float x[8];
-        unpack(xs[i], x);
+        const __half2* h = reinterpret_cast<const __half2*>(&xs[i]);
         uint4 o;
         uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float y0 = fmaf(x[2 * e], scl[2 * e], shf[2 * e]);
-          float y1 = fmaf(x[2 * e + 1], scl[2 * e + 1], shf[2 * e + 1]);
-          if (a.silu) { y0 = silu_f(y0); y1 = silu_f(y1); }
-          ow[e] = pack_half2(y0, y1);
+        for (int j = 0; j < 4; ++j) {
+          const float2 y = fma_f32x2(__half22float2(h[j]), scl2[j], shf2[j]);
+          const uint32_t p = pack_half2(y.x, y.y);
+          ow[j] = a.silu ? silu_h2(p) : p;
         }
         *reinterpret_cast<uint4*>(dst0 + (size_t)i * rows * C) = o;
       }
@@ -395,15 +395,34 @@ int gn_fused_cluster(int C, int groups, int HW, int ns) {
 
 // LayerNorm over C per token: one warp per token, values kept in registers,
 // exact centred variance. Replaces layernorm_f32.comp (vk_engine.cpp:652).
+// Up to five vectors per lane (C <= 1280) the lane's affine parameters are
+// fetched into registers before the programmatic-launch wait (they do not
+// depend on the previous kernel), off the normalisation's critical path.
 template <int VPL>  // 8-channel vectors per lane
 __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, int M, int C, const float* __restrict__ g,
                                                  const float* __restrict__ b, float eps, __half* __restrict__ y) {
-  pdl_wait();
-  pdl_trigger();
+  constexpr bool kPre = VPL <= 5;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= M) return;
   const int nvec = C / 8;
+  float4 gpre[kPre ? VPL * 2 : 1], bpre[kPre ? VPL * 2 : 1];
+  if constexpr (kPre) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        const float4* g4 = reinterpret_cast<const float4*>(g + vi * 8);
+        const float4* b4 = reinterpret_cast<const float4*>(b + vi * 8);
+        gpre[2 * i] = __ldg(g4);
+        gpre[2 * i + 1] = __ldg(g4 + 1);
+        bpre[2 * i] = __ldg(b4);
+        bpre[2 * i + 1] = __ldg(b4 + 1);
+      }
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (warp >= M) return;
   const __half* xr = x + (size_t)warp * C;
   float v[VPL * 8];
   float sum = 0.f;
@@ -446,9 +465,20 @@ __global__ void __launch_bounds__(256) ln_kernel(const __half* __restrict__ x, i
   for (int i = 0; i < VPL; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nvec) {
-      const float4* g4 = reinterpret_cast<const float4*>(g + vi * 8);
-      const float4* b4 = reinterpret_cast<const float4*>(b + vi * 8);
-      const float4 ga = __ldg(g4), gb = __ldg(g4 + 1), ba = __ldg(b4), bb = __ldg(b4 + 1);
+      float4 ga, gb, ba, bb;
+      if constexpr (kPre) {
+        ga = gpre[2 * i];
+        gb = gpre[2 * i + 1];
+        ba = bpre[2 * i];
+        bb = bpre[2 * i + 1];
+      } else {
+        const float4* g4 = reinterpret_cast<const float4*>(g + vi * 8);
+        const float4* b4 = reinterpret_cast<const float4*>(b + vi * 8);
+        ga = __ldg(g4);
+        gb = __ldg(g4 + 1);
+        ba = __ldg(b4);
+        bb = __ldg(b4 + 1);
+      }
       const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
       const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
       uint4 o;
@@ -510,7 +540,11 @@ cudaError_t launch_layernorm(const __half* x, int M, int C, const float* g, cons
   if ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(b)) & 15) return cudaErrorInvalidValue;
   const int nvec = C / 8;
   const int blocks = (M * 32 + 255) / 256;
-  auto k = nvec <= 32 ? ln_kernel<1> : nvec <= 64 ? ln_kernel<2> : nvec <= 128 ? ln_kernel<4> : ln_kernel<8>;
+  auto k = nvec <= 32    ? ln_kernel<1>
+           : nvec <= 64  ? ln_kernel<2>
+           : nvec <= 96  ? ln_kernel<3>
+           : nvec <= 160 ? ln_kernel<5>
+                         : ln_kernel<8>;
   return launch_kernel(k, dim3(blocks), dim3(256), 0, s, 0, x, M, C, g, b, eps, y);
 }
 

@@ -378,4 +378,35 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed fp32 pair arithmetic (PTX .f32x2, sm_100): one instruction for both lanes of a float2,
+// rounded to nearest like the scalar forms.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) { return reinterpret_cast<unsigned long long&>(v); }
+__device__ __forceinline__ float2 f2_from(unsigned long long b) { return reinterpret_cast<float2&>(b); }
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float2 sub_f32x2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from(r);
+}
+// SiLU of both halves of an f16x2, y * (1/2 + tanh(y/2)/2), with one tanh.approx.f16x2 (one MUFU
+// instruction for two values) and half-precision multiplies.
+__device__ __forceinline__ uint32_t silu_h2(uint32_t y) {
+  const __half2 hy = reinterpret_cast<__half2&>(y);
+  const __half2 half = __float2half2_rn(0.5f);
+  const __half2 a = __hmul2(hy, half);
+  uint32_t t;
+  asm("tanh.approx.f16x2 %0, %1;" : "=r"(t) : "r"(reinterpret_cast<const uint32_t&>(a)));
+  const __half2 o = __hmul2(hy, __hfma2(reinterpret_cast<__half2&>(t), half, half));
+  return reinterpret_cast<const uint32_t&>(o);
+}
+
 }  // namespace sdg
