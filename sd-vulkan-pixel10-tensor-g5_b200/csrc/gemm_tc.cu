@@ -362,6 +362,105 @@ __device__ __forceinline__ void epi_apply_rows(const GemmDev& p, int m, int img,
   (void)img;
 }
 
+// Plain fused epilogue of a tile's 32-column chunks owned by one warp, specialised on the operands
+// present (residual, per-image row bias, SiLU, int8 weight scales), so the chunk loop runs
+// straight-line code without per-group branches on the launch arguments. res_next holds the
+// first chunk's residual on entry (loaded before the accumulator wait). Same arithmetic, order of
+// operations and stores as epi_apply_rows.
+template <int BN, int kSplit, bool W8, bool RES, bool ROWB, bool SILU>
+__device__ __forceinline__ void epi_plain_chunks(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
+                                                 int eh, int lane, uint4 (&res_next)[4]) {
+  const int im = mvalid ? img : 0;  // rows past M (last partial tile) must not index past the last image
+  const float* rb_row = ROWB ? p.rowbias + (size_t)im * p.rowbias_ld : nullptr;
+  const __half* res_row = RES ? p.residual + (size_t)m * p.ld_res : nullptr;
+  const int row0 = m - lane + (lane & ~3);  // first row of this lane's quad
+#pragma unroll 1
+  for (int c = eh * 32; c < BN; c += kSplit * 32) {
+    const int n = n0 + c;
+    const int nn = n + kSplit * 32;  // this warp's next chunk
+    if (nn < p.N) {                  // its lines into L1
+      if (p.bias) prefetch_l1(p.bias + nn);
+      if (ROWB) prefetch_l1(rb_row + nn);
+      if (RES && mvalid) prefetch_l1(res_row + nn);
+    }
+    uint32_t r[32];
+    tmem_ld32(t_row + c, r);
+    float4 b[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const bool ok = n + 4 * q < p.N;
+      b[q] = (ok && p.bias) ? __ldg(reinterpret_cast<const float4*>(p.bias + n) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ROWB && ok) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(rb_row + n) + q);
+        b[q].x += t.x; b[q].y += t.y; b[q].z += t.z; b[q].w += t.w;
+      }
+    }
+    uint4 res[4];
+    if constexpr (RES) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) res[g] = res_next[g];
+      if (c + kSplit * 32 < BN) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          res_next[g] = (mvalid && nn + 8 * g < p.N) ? __ldg(reinterpret_cast<const uint4*>(res_row + nn) + g)
+                                                    : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    tmem_wait_ld();
+    if (n >= p.N) continue;  // (the same for every lane of the warp)
+    uint4 o[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+      if constexpr (W8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + n + g * 8 + j);
+      }
+      const float4 b0 = b[2 * g], b1 = b[2 * g + 1];
+      v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+      v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+      if constexpr (RES) {
+        const __half2* h = reinterpret_cast<const __half2*>(&res[g]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h[e]);
+          v[2 * e] += f.x;
+          v[2 * e + 1] += f.y;
+        }
+      }
+      if constexpr (SILU) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
+      }
+      o[g] = pack8(v);
+    }
+    quad_transpose(o, lane);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int mr = row0 + i;
+      if (mr < p.M) *reinterpret_cast<uint4*>(p.out + (size_t)mr * p.ld_out + n + 8 * (lane & 3)) = o[i];
+    }
+  }
+}
+
+template <int BN, int kSplit, bool W8>
+__device__ __forceinline__ void epi_plain_dispatch(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
+                                                   int eh, int lane, uint4 (&res_next)[4]) {
+  const int sel = (p.residual ? 1 : 0) | (p.rowbias ? 2 : 0) | (p.act == 1 ? 4 : 0);
+  switch (sel) {
+    case 0: epi_plain_chunks<BN, kSplit, W8, false, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 1: epi_plain_chunks<BN, kSplit, W8, true, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 2: epi_plain_chunks<BN, kSplit, W8, false, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 3: epi_plain_chunks<BN, kSplit, W8, true, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 4: epi_plain_chunks<BN, kSplit, W8, false, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 5: epi_plain_chunks<BN, kSplit, W8, true, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 6: epi_plain_chunks<BN, kSplit, W8, false, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    default: epi_plain_chunks<BN, kSplit, W8, true, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+  }
+}
+
 // int8 x4 (one 32-bit word) -> two fp16x2, exact: bias the bytes to unsigned,
 // splice each under the fp16 exponent of 1024 (0x64), subtract 1024 + 128.
 __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& hi) {
@@ -375,7 +474,11 @@ __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& h
   hi = *reinterpret_cast<uint32_t*>(&hb);
 }
 
-template <int BN, bool W8, bool PAIR>
+// PLAIN: the instantiation for single-pass launches with a plain fp16 output (no K split, no
+// GEGLU / attention-head / NCHW epilogue), whose epilogue is epi_plain_dispatch alone; the other
+// instantiation carries every epilogue and K-split form. Keeping them apart keeps the plain path
+// free of the other paths' register pressure and code.
+template <int BN, bool W8, bool PAIR, bool PLAIN>
 __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_w, const GemmDev p) {
@@ -385,7 +488,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
   // cluster K split (1-CTA tiles only): the csp CTAs of a cluster share one output tile, CTA krank
   // computes the k-blocks [krank * kb_per_split, ...) and the partial tiles are summed through
   // distributed shared memory; one tile per cluster (no persistent loop)
-  const int csp = PAIR ? 1 : p.csplit;
+  const int csp = (PAIR || PLAIN) ? 1 : p.csplit;
   const int krank = csp > 1 ? (int)cluster_ctarank() : 0;
   const int team = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x / csp;  // pair / cluster / CTA index
   const int nteams = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x / csp;
@@ -657,7 +760,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
       constexpr int CH = C::kChunk;
-      if (csp > 1) {
+      if constexpr (PLAIN) {
+        static_assert(CH == 32, "the plain epilogue walks 32-column chunks");
+        epi_plain_dispatch<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh, lane, res_next);
+      } else if (csp > 1) {
         // cluster K split: the partial tile stays in TMEM until every CTA of the cluster is
         // past its main loop (reduction below)
       } else if (p.epi == kEpiGeglu) {
@@ -866,28 +972,40 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
   }
 }
 
-template <int BN, bool W8, bool PAIR>
-cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1, const CUtensorMap& mw,
-                      cudaStream_t s) {
-  using C = Cfg<BN, W8, PAIR>;
+template <int BN, bool W8, bool PAIR, bool PLAIN>
+cudaError_t set_gemm_smem() {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, PLAIN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN, W8, PAIR>::kSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
+  return cudaSuccess;
+}
+
+template <int BN, bool W8, bool PAIR>
+cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMap& ma1, const CUtensorMap& mw,
+                      cudaStream_t s) {
+  using C = Cfg<BN, W8, PAIR>;
   constexpr int TM = PAIR ? 2 * BM : BM;
   const int tiles = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN);
-  if (!PAIR && d.csplit > 1)  // one cluster of csplit CTAs per output tile
-    return launch_kernel(gemm_tc_kernel<BN, W8, PAIR>, dim3(tiles * d.csplit), dim3(C::kThreads), C::kSmem, s,
+  if (!PAIR && d.csplit > 1) {  // one cluster of csplit CTAs per output tile
+    cudaError_t e = set_gemm_smem<BN, W8, PAIR, false>();
+    if (e != cudaSuccess) return e;
+    return launch_kernel(gemm_tc_kernel<BN, W8, PAIR, false>, dim3(tiles * d.csplit), dim3(C::kThreads), C::kSmem, s,
                          d.csplit, ma0, ma1, mw, d);
+  }
   const int units = tiles * d.splits;
   const int teams = std::max(1, std::min(units, PAIR ? num_sms() / 2 : num_sms()));
-  cudaError_t e = launch_kernel(gemm_tc_kernel<BN, W8, PAIR>, dim3(PAIR ? 2 * teams : teams), dim3(C::kThreads),
-                                C::kSmem, s, PAIR ? 2 : 0, ma0, ma1, mw, d);
+  constexpr bool kCanPlain = C::kChunk == 32;
+  const bool plain = kCanPlain && d.splits == 1 && d.epi == kEpiPlain;
+  cudaError_t e = plain ? set_gemm_smem<BN, W8, PAIR, kCanPlain>() : set_gemm_smem<BN, W8, PAIR, false>();
+  if (e != cudaSuccess) return e;
+  e = launch_kernel(plain ? gemm_tc_kernel<BN, W8, PAIR, kCanPlain> : gemm_tc_kernel<BN, W8, PAIR, false>,
+                    dim3(PAIR ? 2 * teams : teams), dim3(C::kThreads), C::kSmem, s, PAIR ? 2 : 0, ma0, ma1, mw, d);
   if (e != cudaSuccess || d.splits == 1) return e;
   const size_t total = (size_t)d.M * ((d.N + 7) / 8);
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
@@ -937,7 +1055,7 @@ int cluster_capacity(int cs) {
   if (dev >= 64 || cs < 2 || cs > kMaxCsplitCtas) return std::max(1, num_sms() / std::max(1, cs));
   if (!known[dev][cs]) {
     using C = Cfg<160, false, false>;
-    auto k = gemm_tc_kernel<160, false, false>;
+    auto k = gemm_tc_kernel<160, false, false, false>;
     int n = 0;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
