@@ -43,6 +43,13 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kMaxCsplitCtas = 8;  // cluster K split: at most the portable cluster size
+// epilogue kinds of the kernel instantiations (gemm_tc_kernel's EK)
+constexpr int kEkGeneric = 0, kEkPlain = 1, kEkHeads = 3;
+// Epilogue warps: two per TMEM lane quadrant (10 warps in all: at most three per SM sub-partition,
+// 168 registers a thread); wo8 four epilogue and four int8 converter warps. (Three per quadrant, 14
+// warps at 128 registers, measured no faster on B200.)
+constexpr int gemm_epi_warps(bool w8, int ek) { return (void)ek, w8 ? 4 : 8; }
+constexpr int gemm_threads(bool w8, int ek) { return 64 + 32 * (gemm_epi_warps(w8, ek) + (w8 ? 4 : 0)); }
 constexpr uint32_t kATileBytes = BM * BK * 2;  // 16 KB
 
 struct GemmDev {
@@ -83,8 +90,8 @@ struct Cfg {
   static_assert(!(W8 && PAIR), "weight-only int8 tiles use single-CTA kernels");
   // warps: 0 TMA, 1 MMA, then 8 epilogue warps (two per TMEM lane quadrant, alternating
   // column chunks), or for wo8 4 epilogue warps + 4 int8 converter warps
-  static constexpr int kThreads = 320;
-  static constexpr int kEpiWarps = W8 ? 4 : 8;
+  static constexpr int kThreads = gemm_threads(W8, kEkGeneric);  // of the generic instantiation
+  static constexpr int kEpiWarps = gemm_epi_warps(W8, kEkGeneric);
   static constexpr int kBRows = PAIR ? BN / 2 : BN;  // W rows held by this CTA
   static constexpr uint32_t kBTileBytes = kBRows * BK * 2;
   static constexpr uint32_t kB8Bytes = W8 ? BN * BK : 0;  // int8 staging tile
@@ -461,6 +468,56 @@ __device__ __forceinline__ void epi_plain_dispatch(const GemmDev& p, uint32_t t_
   }
 }
 
+// Attention-head epilogue (Q / K / V projections: bias, no residual, no activation) of a warp's
+// 32-column chunks: scatter into the padded per-head layouts, V (head_vt) transposed.
+template <int BN, int kSplit, bool W8>
+__device__ __forceinline__ void epi_heads_chunks(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
+                                                 int eh) {
+  const int s_idx = m - img * p.rows_per_image;
+#pragma unroll 1
+  for (int c = eh * 32; c < BN; c += kSplit * 32) {
+    const int n = n0 + c;
+    if (p.bias && n + kSplit * 32 < p.N) prefetch_l1(p.bias + n + kSplit * 32);
+    uint32_t r[32];
+    tmem_ld32(t_row + c, r);
+    float4 b[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      b[q] = (p.bias && n + 4 * q < p.N) ? __ldg(reinterpret_cast<const float4*>(p.bias + n) + q)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    tmem_wait_ld();
+    if (!mvalid || n >= p.N) continue;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int ng = n + g * 8;
+      if (ng >= p.N) break;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+      if constexpr (W8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + ng + j);
+      }
+      const float4 b0 = b[2 * g], b1 = b[2 * g + 1];
+      v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+      v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+      const int which = ng / p.head_C;
+      const int cc = ng - which * p.head_C;
+      const int h = cc / p.head_d;
+      const int jj = cc - h * p.head_d;
+      __half* base = which == 0 ? p.head_out0 : (which == 1 ? p.head_out1 : p.head_out2);
+      if (which == p.head_vt) {  // consecutive rows of the warp are consecutive keys
+        __half* dst = base + (((size_t)img * p.heads + h) * p.head_d16 + jj) * p.head_spad + s_idx;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dst[(size_t)e * p.head_spad] = __float2half_rn(v[e]);
+        continue;
+      }
+      __half* dst = base + (((size_t)img * p.heads + h) * p.rows_per_image + s_idx) * p.head_dp + jj;
+      *reinterpret_cast<uint4*>(dst) = pack8(v);
+    }
+  }
+}
+
 // int8 x4 (one 32-bit word) -> two fp16x2, exact: bias the bytes to unsigned,
 // splice each under the fp16 exponent of 1024 (0x64), subtract 1024 + 128.
 __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& hi) {
@@ -474,21 +531,23 @@ __device__ __forceinline__ void i8x4_to_h4(uint32_t w, uint32_t& lo, uint32_t& h
   hi = *reinterpret_cast<uint32_t*>(&hb);
 }
 
-// PLAIN: the instantiation for single-pass launches with a plain fp16 output (no K split, no
-// GEGLU / attention-head / NCHW epilogue), whose epilogue is epi_plain_dispatch alone; the other
-// instantiation carries every epilogue and K-split form. Keeping them apart keeps the plain path
-// free of the other paths' register pressure and code.
-template <int BN, bool W8, bool PAIR, bool PLAIN>
-__global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
+// EK: the epilogue this instantiation carries. Single-pass launches (no K split) with a plain fp16
+// output or attention-head outputs (no residual, no activation) run an instantiation with that
+// epilogue alone (kEkPlain / kEkHeads); kEkGeneric carries every epilogue (GEGLU included: its
+// own instantiation measured slower on B200) and both K-split forms. Keeping them apart keeps each
+// path free of the others' register pressure, code and branches.
+template <int BN, bool W8, bool PAIR, int EK>
+__global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_w, const GemmDev p) {
   using C = Cfg<BN, W8, PAIR>;
+  constexpr int kEpiW = gemm_epi_warps(W8, EK);
   constexpr int TM = PAIR ? 2 * BM : BM;  // output rows per unit
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   // cluster K split (1-CTA tiles only): the csp CTAs of a cluster share one output tile, CTA krank
   // computes the k-blocks [krank * kb_per_split, ...) and the partial tiles are summed through
   // distributed shared memory; one tile per cluster (no persistent loop)
-  const int csp = (PAIR || PLAIN) ? 1 : p.csplit;
+  const int csp = (PAIR || EK != kEkGeneric) ? 1 : p.csplit;
   const int krank = csp > 1 ? (int)cluster_ctarank() : 0;
   const int team = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x / csp;  // pair / cluster / CTA index
   const int nteams = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x / csp;
@@ -540,7 +599,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), C::kEpiWarps * (PAIR ? 2 : 1));  // epilogue warps of both CTAs arrive on the even CTA's
+      mbar_init(tempty_bar(a), kEpiW * (PAIR ? 2 : 1));  // epilogue warps of both CTAs arrive on the even CTA's
     }
     mbar_init(drain_bar, 1);
     if constexpr (W8)
@@ -569,7 +628,11 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();  // the previous kernel's outputs are visible from here on
+  // Programmatic launch: the next kernel may be scheduled now (its own wait orders its accesses).
+  // The roles that touch global memory wait for the previous kernel themselves, as late as they
+  // can: the producer just before its first copy (its setup overlaps the previous kernel's tail),
+  // the epilogue warps before their first load. The MMA issuer and the wo8 converters work on
+  // shared memory and TMEM only, ordered after the producer's copies by the mbarriers.
   pdl_trigger();
 
   if (warp == 0) {
@@ -579,7 +642,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       int last_phase[S];
       bool issued[S];
       for (int s = 0; s < S; ++s) { issued[s] = false; last_phase[s] = 0; }
-      bool ok = true;
+      bool ok = true, waited = false;
       for (int unit = team; unit < num_units && ok; unit += nteams) {
         int m_blk, n_blk, kb0, kb1;
         decode(unit, m_blk, n_blk, kb0, kb1);
@@ -597,6 +660,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
           const int nsub = min(G, kb1 - kb);  // k-blocks in this stage (the unit's last may be short)
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.err, kDevTimeoutEmpty, p.wait_ns)) { ok = false; break; }
           if ((int)it == p.stall_it) continue;  // failure-path test: this stage is never loaded
+          if (!waited) {
+            pdl_wait();  // the previous kernel's outputs are visible from here on
+            waited = true;
+          }
           if (rank == 0) mbar_arrive_expect_tx(full_bar(s), (uint32_t)nsub * C::kTxBytes);
           issued[s] = true;
           last_phase[s] = ph;
@@ -737,9 +804,10 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // residual / bias reads and the output stores come after the previous kernel
     const int lg = warp & 3;  // TMEM lane group this warp may access
     const int row = lg * 32 + lane;
-    constexpr int kSplit = C::kEpiWarps / 4;  // warps sharing a lane quadrant split its column chunks
+    constexpr int kSplit = kEpiW / 4;  // warps sharing a lane quadrant split its column chunks
     const int eh = (warp - 2) >> 2;
     uint32_t tl = 0;
     for (int unit = team; unit < num_units; unit += nteams, ++tl) {
@@ -760,9 +828,11 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * C::kAccStride + (static_cast<uint32_t>(lg * 32) << 16);
       constexpr int CH = C::kChunk;
-      if constexpr (PLAIN) {
-        static_assert(CH == 32, "the plain epilogue walks 32-column chunks");
+      if constexpr (EK != kEkGeneric) static_assert(CH == 32, "the specialised epilogues walk 32-column chunks");
+      if constexpr (EK == kEkPlain) {
         epi_plain_dispatch<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh, lane, res_next);
+      } else if constexpr (EK == kEkHeads) {
+        epi_heads_chunks<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh);
       } else if (csp > 1) {
         // cluster K split: the partial tile stays in TMEM until every CTA of the cluster is
         // past its main loop (reduction below)
@@ -876,14 +946,14 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
     // the fused epilogue. Stage memory is reused, so the pushes start only once every CTA of
     // the cluster is past its main loop.
     const int rpc = (BM + csp - 1) / csp;
-    const bool epi_warp = warp >= 2 && warp < 2 + C::kEpiWarps && team < num_units;
+    const bool epi_warp = warp >= 2 && warp < 2 + kEpiW && team < num_units;
     tc_fence_before();
     cluster_sync_all();
     if (epi_warp) {
       tc_fence_after();
       const int lg = warp & 3;
       const int row = lg * 32 + lane;
-      constexpr int kSplit = C::kEpiWarps / 4;
+      constexpr int kSplit = kEpiW / 4;
       const int eh = (warp - 2) >> 2;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(lg * 32) << 16);
       const int owner = row / rpc;
@@ -914,7 +984,7 @@ __global__ void __launch_bounds__(Cfg<BN, W8, PAIR>::kThreads, 1)
       const int r0 = krank * rpc, nrows = min(rpc, BM - r0);
       const int ngrp = BN / 8;
       const float* buf = reinterpret_cast<const float*>(smem);
-      for (int i = threadIdx.x - 64; i < nrows * ngrp; i += C::kEpiWarps * 32) {
+      for (int i = threadIdx.x - 64; i < nrows * ngrp; i += kEpiW * 32) {
         const int rl = i / ngrp;
         const int c = (i % ngrp) * 8;
         const int m = m_blk * BM + r0 + rl;
@@ -972,13 +1042,13 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmDev p) {
   }
 }
 
-template <int BN, bool W8, bool PAIR, bool PLAIN>
+template <int BN, bool W8, bool PAIR, int EK>
 cudaError_t set_gemm_smem() {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, PLAIN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, EK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN, W8, PAIR>::kSmem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
@@ -993,19 +1063,31 @@ cudaError_t launch_bn(const GemmDev& d, const CUtensorMap& ma0, const CUtensorMa
   constexpr int TM = PAIR ? 2 * BM : BM;
   const int tiles = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN);
   if (!PAIR && d.csplit > 1) {  // one cluster of csplit CTAs per output tile
-    cudaError_t e = set_gemm_smem<BN, W8, PAIR, false>();
+    cudaError_t e = set_gemm_smem<BN, W8, PAIR, kEkGeneric>();
     if (e != cudaSuccess) return e;
-    return launch_kernel(gemm_tc_kernel<BN, W8, PAIR, false>, dim3(tiles * d.csplit), dim3(C::kThreads), C::kSmem, s,
-                         d.csplit, ma0, ma1, mw, d);
+    return launch_kernel(gemm_tc_kernel<BN, W8, PAIR, kEkGeneric>, dim3(tiles * d.csplit), dim3(C::kThreads), C::kSmem,
+                         s, d.csplit, ma0, ma1, mw, d);
   }
   const int units = tiles * d.splits;
   const int teams = std::max(1, std::min(units, PAIR ? num_sms() / 2 : num_sms()));
-  constexpr bool kCanPlain = C::kChunk == 32;
-  const bool plain = kCanPlain && d.splits == 1 && d.epi == kEpiPlain;
-  cudaError_t e = plain ? set_gemm_smem<BN, W8, PAIR, kCanPlain>() : set_gemm_smem<BN, W8, PAIR, false>();
+  // the epilogue-specialised instantiations exist for 32-column chunks (every width but 16)
+  constexpr bool kSpec = C::kChunk == 32;
+  int ek = kEkGeneric;
+  if (kSpec && d.splits == 1) {
+    if (d.epi == kEpiPlain) ek = kEkPlain;
+    else if (d.epi == kEpiHeads && !d.residual && d.act == 0) ek = kEkHeads;
+  }
+  constexpr int kP = kSpec ? kEkPlain : kEkGeneric, kH = kSpec ? kEkHeads : kEkGeneric;
+  auto kern = ek == kEkPlain   ? gemm_tc_kernel<BN, W8, PAIR, kP>
+              : ek == kEkHeads ? gemm_tc_kernel<BN, W8, PAIR, kH>
+                               : gemm_tc_kernel<BN, W8, PAIR, kEkGeneric>;
+  cudaError_t e = ek == kEkPlain   ? set_gemm_smem<BN, W8, PAIR, kP>()
+                  : ek == kEkHeads ? set_gemm_smem<BN, W8, PAIR, kH>()
+                                   : set_gemm_smem<BN, W8, PAIR, kEkGeneric>();
   if (e != cudaSuccess) return e;
-  e = launch_kernel(plain ? gemm_tc_kernel<BN, W8, PAIR, kCanPlain> : gemm_tc_kernel<BN, W8, PAIR, false>,
-                    dim3(PAIR ? 2 * teams : teams), dim3(C::kThreads), C::kSmem, s, PAIR ? 2 : 0, ma0, ma1, mw, d);
+  const int kern_ek = ek == kEkPlain ? kP : ek == kEkHeads ? kH : kEkGeneric;
+  e = launch_kernel(kern, dim3(PAIR ? 2 * teams : teams), dim3(gemm_threads(W8, kern_ek)), C::kSmem, s, PAIR ? 2 : 0,
+                    ma0, ma1, mw, d);
   if (e != cudaSuccess || d.splits == 1) return e;
   const size_t total = (size_t)d.M * ((d.N + 7) / 8);
   const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
@@ -1055,7 +1137,7 @@ int cluster_capacity(int cs) {
   if (dev >= 64 || cs < 2 || cs > kMaxCsplitCtas) return std::max(1, num_sms() / std::max(1, cs));
   if (!known[dev][cs]) {
     using C = Cfg<160, false, false>;
-    auto k = gemm_tc_kernel<160, false, false, false>;
+    auto k = gemm_tc_kernel<160, false, false, kEkGeneric>;
     int n = 0;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
