@@ -177,7 +177,9 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();  // the previous kernel's outputs (Q/K/V) are visible from here on
+  // Programmatic launch: the next kernel may be scheduled now. The producer waits for the previous
+  // kernel's outputs (Q/K/V) just before its first copy, the softmax warps before their stores; the
+  // MMA issuer works on shared memory and TMEM only, ordered by the mbarriers.
   pdl_trigger();
 
   if (warp == 0) {
@@ -185,6 +187,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
+      pdl_wait();  // the previous kernel's outputs are visible from here on
       mbar_arrive_expect_tx(q_full, NQT * CF::kQTile);
       for (int t = 0; t < NQT; ++t)
         for (int a = 0; a < NATOM; ++a)
@@ -321,6 +324,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     }
   } else if constexpr (CF::TPV) {
     // ---------------------------------------------------------------- softmax, transposed PV
+    pdl_wait();
     // As the per-tile path below, but O^T accumulates in TMEM for both tiles: d row r of the
     // M=64 accumulator sits in lane (r % 16) + 32 (r / 16), query row `row` of tile t in column
     // 128 t + row. A row-max raise rescales that row's O^T column across all 64 lanes, so the
@@ -449,6 +453,7 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax
+    pdl_wait();
     // O accumulates in TMEM (PV with accumulate); a row's running max is only
     // raised when a new score exceeds it by more than 2^8 (then that O row and l
     // are rescaled through tcgen05.ld/st), so P <= 256 always fits fp16 and the
