@@ -277,6 +277,21 @@ SDG_API int sdg_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* y,
 SDG_API int sdg_concat(const uint16_t* a, int Ca, const uint16_t* b, int Cb, int rows, uint16_t* y, void* stream);
 SDG_API int sdg_upsample2x(const uint16_t* x, int B, int H, int W, int C, uint16_t* y, void* stream);
 
+/* Replaces the reference's upsample() block (vk_engine.cpp:693-697: upsample_f32.comp nearest 2x, then
+ * a 3x3 pad-1 conv) with one implicit GEMM that never writes the upsampled tensor: each output phase
+ * (py, px) of the 2H x 2W output is a 2x2 convolution of the H x W input with folded weights.
+ * Host-only (no GPU): folds a 3x3 kernel w3 [Co][Ci][3][3] (the reference's conv layout, fp16 bits)
+ * into wp [4 phases][Co][4 taps][Ci] (ph = 2 py + px, tap = 2 ty + tx): the fp32 sum of the 3x3 taps
+ * that land on input pixel (i + ty + py - 1, j + tx + px - 1) of output pixel (2i + py, 2j + px),
+ * rounded once to fp16. 16 * Co * Ci values. */
+SDG_API int sdg_pack_upsample_conv_weights(const uint16_t* w3, int Co, int Ci, uint16_t* wp);
+/* y [B,2H,2W,Co] = conv3x3(upsample2x(x)) + bias, x [B,H,W,Ci] (Ci and Co multiples of 64), wp from
+ * sdg_pack_upsample_conv_weights, bias4 the conv bias repeated per phase [4 * Co] (fp32, may be NULL).
+ * workspace as in sdg_conv2d. */
+SDG_API int sdg_upsample_conv3x3(const uint16_t* x, int B, int H, int W, int Ci, const uint16_t* wp,
+                                 const float* bias4, int Co, uint16_t* y, void* workspace, size_t workspace_bytes,
+                                 int* err_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

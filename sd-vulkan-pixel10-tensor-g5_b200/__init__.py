@@ -96,6 +96,8 @@ _SIGS = {
     "sdg_add": (_I, [_P, _P, ctypes.c_size_t, _P, _P]),
     "sdg_concat": (_I, [_P, _I, _P, _I, _I, _P, _P]),
     "sdg_upsample2x": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "sdg_pack_upsample_conv_weights": (_I, [_P, _I, _I, _P]),
+    "sdg_upsample_conv3x3": (_I, [_P, _I, _I, _I, _I, _P, _P, _I, _P, _P, ctypes.c_size_t, _P, _P]),
 }
 
 
@@ -416,6 +418,33 @@ def upsample2x(x, out=None, stream=None):
     if out is None:
         out = torch.empty((B, 2 * H, 2 * W, C), dtype=x.dtype, device=x.device)
     check(lib().sdg_upsample2x(_ptr(x), B, H, W, C, _ptr(out), _stream(stream)))
+    return out
+
+
+def pack_upsample_conv_weight(w3):
+    """3x3 conv weight [Co,Ci,3,3] (fp16 numpy array or CPU tensor) -> the folded phase weights
+    [4 phases][Co][4 taps][Ci] of ``upsample_conv3x3`` (host-side, through the C ABI)."""
+    import numpy as np
+    w = np.ascontiguousarray(np.asarray(w3, dtype=np.float16))
+    Co, Ci = w.shape[0], w.shape[1]
+    assert w.shape == (Co, Ci, 3, 3), w.shape
+    out = np.empty((4, Co, 4, Ci), dtype=np.float16)
+    check(lib().sdg_pack_upsample_conv_weights(w.ctypes.data, Co, Ci, out.ctypes.data))
+    return out
+
+
+def upsample_conv3x3(x, wp, bias4, out=None, workspace=None, err_word=None, stream=None):
+    """conv3x3(upsample2x(x)) + bias without the upsampled copy: x [B,H,W,Ci] fp16, wp the folded phase
+    weights [4,Co,4,Ci] fp16 (pack_upsample_conv_weight, on the device), bias4 fp32 [4*Co] (the conv bias
+    repeated per phase) or None; returns [B,2H,2W,Co]."""
+    import torch
+    B, H, W, Ci = x.shape
+    Co = wp.shape[1]
+    if out is None:
+        out = torch.empty((B, 2 * H, 2 * W, Co), dtype=torch.float16, device=x.device)
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().sdg_upsample_conv3x3(_ptr(x), B, H, W, Ci, _ptr(wp), _ptr(bias4), Co, _ptr(out), _ptr(workspace), wsb,
+                                     _ptr(err_word), _stream(stream)))
     return out
 
 

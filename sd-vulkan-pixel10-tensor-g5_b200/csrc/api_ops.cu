@@ -127,6 +127,31 @@ SDG_API int sdg_conv2d(const uint16_t* x, const uint16_t* x2, int B, int H, int 
   return cuda_status(sdg::launch_gemm(a, err, s), "conv2d");
 }
 
+SDG_API int sdg_pack_upsample_conv_weights(const uint16_t* w3, int Co, int Ci, uint16_t* wp) {
+  if (!w3 || !wp || Co <= 0 || Ci <= 0) return sdg::op_fail(SDG_ERR_ARG, "pack_upsample_conv_weights: bad arguments");
+  sdg::pack_upsample_conv_weights(w3, Co, Ci, wp);
+  return SDG_OK;
+}
+
+SDG_API int sdg_upsample_conv3x3(const uint16_t* x, int B, int H, int W, int Ci, const uint16_t* wp,
+                                 const float* bias4, int Co, uint16_t* y, void* workspace, size_t workspace_bytes,
+                                 int* err_word, void* stream) {
+  if (!x || !wp || !y || B <= 0 || H <= 0 || W <= 0 || Ci <= 0 || Co <= 0)
+    return sdg::op_fail(SDG_ERR_ARG, "upsample_conv3x3: bad arguments");
+  if (Ci % 64 || Co % 64) return sdg::op_fail(SDG_ERR_SHAPE, "upsample_conv3x3: Ci and Co must be multiples of 64");
+  sdg::GemmArgs a;
+  a.M = B * H * W; a.N = 4 * Co; a.K = 4 * Ci; a.taps = 4; a.up_co = Co;
+  a.a0 = reinterpret_cast<const __half*>(x); a.cin0 = Ci;
+  a.B = B; a.H = H; a.W = W; a.rows_per_image = H * W;
+  a.w = reinterpret_cast<const __half*>(wp);
+  a.bias = bias4;
+  a.out = reinterpret_cast<__half*>(y);
+  a.ws = static_cast<float*>(workspace);
+  a.ws_bytes = workspace ? workspace_bytes : 0;
+  return cuda_status(sdg::launch_gemm(a, err_word ? err_word : internal_err_word(), static_cast<cudaStream_t>(stream)),
+                     "upsample_conv3x3");
+}
+
 static int linear_common(const char* name, const uint16_t* x, int M, int K, const uint16_t* w, const int8_t* w8,
                          const float* wscale, const float* bias, int N, const uint16_t* residual, int act, uint16_t* y,
                          void* workspace, size_t workspace_bytes, int* err_word, void* stream) {

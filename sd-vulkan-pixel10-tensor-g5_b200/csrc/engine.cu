@@ -60,6 +60,9 @@ struct Lin { __half* w = nullptr; float* b = nullptr; int N = 0, K = 0; int8_t* 
 struct Norm { float* g = nullptr; float* b = nullptr; int C = 0; };
 struct ConvW {
   __half* w = nullptr; float* b = nullptr; int Co = 0, Ci = 0, k = 3; int8_t* w8 = nullptr; float* ws = nullptr;
+  // upsampler conv on fp16 weights: w = [4 phases * Co][4 taps][Ci] (2x2 phase convolutions of the
+  // low-resolution input), b = the bias repeated per phase [4 * Co]
+  bool up = false;
 };
 struct ResW { Norm n1, n2; ConvW c1, c2; bool has_sc = false; Lin sc; int tp_off = 0, cin = 0, cout = 0; };
 struct TfW { Norm gn, ln1, ln2, ln3; Lin pin, qkv, out1, q2, kv2, out2, ff1, ff2, pout; int C = 0; };
@@ -368,6 +371,24 @@ struct WeightPacker {
           d[((size_t)oc * k * k + t) * ci + ic] = hw ? hw->data[((size_t)oc * ci + ic) * k * k + t] : 0;
     vecf(&c.b, pf + ".bias", co);
   }
+  // Upsampler conv (nearest 2x then 3x3 pad 1) as four 2x2 phase convolutions of the low-resolution
+  // input: weights folded per output phase (pack_upsample_conv_weights), bias repeated per phase.
+  // fp16 weights only (the weight-only int8 engine keeps the explicit upsample and the 3x3 conv).
+  void conv_upsample(ConvW& c, const std::string& pf, int ci, int co) {
+    c.Co = co; c.Ci = ci; c.k = 3; c.up = true;
+    const size_t o = reserve((size_t)4 * co * 4 * ci * 2);
+    place(&c.w, o);
+    const HostWeight* hw = get(pf + ".weight", (size_t)co * ci * 9);
+    uint16_t* d = reinterpret_cast<uint16_t*>(staging.data() + o);
+    if (hw) pack_upsample_conv_weights(hw->data.data(), co, ci, d);
+    else std::fill(d, d + (size_t)16 * co * ci, uint16_t(0));
+    const size_t bo = reserve((size_t)4 * co * 4);
+    place(&c.b, bo);
+    const HostWeight* hb = get(pf + ".bias", co);
+    float* bd = reinterpret_cast<float*>(staging.data() + bo);
+    for (int q = 0; q < 4; ++q)
+      for (int i = 0; i < co; ++i) bd[q * co + i] = hb ? h2f(hb->data[i]) : 0.f;
+  }
   void conv1x1_as_linear(Lin& L, const std::string& pf, int ci, int co) {
     ConvW c;
     conv(c, pf, ci, co, 1);
@@ -509,7 +530,10 @@ int Engine::prepare() {
       }
       if (i < 3) {
         snprintf(pf, sizeof pf, "up_blocks.%d.upsamplers.0.conv", i);
-        P.conv(w.up_us[i], pf, up_out[i], up_out[i], 3);
+        if (wo8)
+          P.conv(w.up_us[i], pf, up_out[i], up_out[i], 3);
+        else
+          P.conv_upsample(w.up_us[i], pf, up_out[i], up_out[i]);
       }
     }
   }
@@ -605,8 +629,9 @@ void Builder::gn(const Buf& x, const Buf* x2, int B, int HW, const Norm& n, floa
 // nine taps), the weights, the output and the residual.
 static double gemm_algorithmic_bytes(const GemmArgs& a) {
   const double cin = a.cin0 + a.cin1;
-  const double in = 2.0 * a.M * (a.taps == 9 ? cin : (double)a.K);
+  const double in = 2.0 * a.M * (a.taps != 1 ? cin : (double)a.K);  // a convolution reads its input once
   const double wt = (a.w8 ? 1.0 : 2.0) * a.N * a.K + (a.w8 ? 4.0 * a.N : 0.0);
+  // (the upsample conv's N counts its four output phases: 2 M N bytes are its [B, 2H, 2W, Co] output)
   const double out = a.epi == kEpiNchwF32 ? 4.0 * a.M * a.N : 2.0 * a.M * (a.epi == kEpiGeglu ? a.N / 2 : a.N);
   const double res = a.residual ? 2.0 * a.M * a.N : 0.0;
   return in + wt + out + res;
@@ -806,6 +831,17 @@ Buf Builder::downsample(const ConvW& c, const Buf& x, int H, int W) {
 Buf Builder::upsample(const ConvW& c, const Buf& x, int H, int W) {
   const int B = pl_.B, Ho = 2 * H, Wo = 2 * W, M = B * Ho * Wo;
   Buf out{alloc_h((size_t)M * c.Co), c.Co};
+  if (c.up) {
+    // nearest 2x + 3x3 conv (vk_engine.cpp:693-697) as one implicit GEMM over the low-resolution input:
+    // each output phase (py, px) is a 2x2 convolution with folded weights (16 of the 36 taps' work), and
+    // the epilogue scatters phase rows onto the 2H x 2W output; no upsampled copy is written
+    GemmArgs a;
+    a.M = B * H * W; a.N = 4 * c.Co; a.K = 4 * x.C; a.taps = 4; a.up_co = c.Co; a.a0 = x.p; a.cin0 = x.C;
+    a.B = B; a.H = H; a.W = W; a.rows_per_image = H * W;
+    a.w = c.w; a.bias = c.b; a.out = out.p;
+    gemm(a, kCatConv3);
+    return out;
+  }
   const size_t mark = off_;
   __half* up = alloc_h((size_t)M * x.C);
   if (!dry_ && ok()) {

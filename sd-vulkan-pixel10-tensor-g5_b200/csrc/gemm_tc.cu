@@ -57,6 +57,7 @@ struct GemmDev {
   int taps, cin0, cin1;
   int H, W;                // conv geometry (input image)
   int cs;                  // conv stride (1 or 2): output Ho = H / cs, Wo = W / cs
+  int up_w, up_co;         // taps == 4 (upsample conv): input width, output channels per phase; else 0
   int epi, act;
   const float* bias;
   const float* rowbias;
@@ -156,6 +157,19 @@ __device__ __forceinline__ void add8_f32(const float* src, float (&v)[8]) {  // 
   v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
 }
 
+// Address of output element (m, n) of a plain fp16 output. For the taps == 4 upsample convolution,
+// GEMM row m is input pixel (I, j) (I = m / W counting rows of all images, j = m % W) and column n is
+// channel c of phase ph = 2 py + px (n = ph * up_co + c); it lands on output pixel (2I + py, 2j + px)
+// of the [2I', 2W] NHWC output, i.e. output row 2 m + 2 W I + 2 W py + px.
+__device__ __forceinline__ __half* out_at(const GemmDev& p, int m, int n) {
+  if (p.up_w) {
+    const int ph = n / p.up_co;
+    const int orow = 2 * m + 2 * p.up_w * (m / p.up_w + (ph >> 1)) + (ph & 1);
+    return p.out + (size_t)orow * p.ld_out + (n - ph * p.up_co);
+  }
+  return p.out + (size_t)m * p.ld_out + n;
+}
+
 // Fused epilogue for 8 consecutive output columns [n, n+8) of row m (m < M) of
 // image img = m / rows_per_image. Not used for GEGLU (which pairs two column ranges).
 __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int img, int n, float (&v)[8]) {
@@ -201,7 +215,7 @@ __device__ __forceinline__ void epilogue8(const GemmDev& p, int m, int img, int 
     *reinterpret_cast<uint4*>(dst) = pack8(v);
     return;
   }
-  *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + n) = pack8(v);
+  *reinterpret_cast<uint4*>(out_at(p, m, n)) = pack8(v);
 }
 
 // Epilogue operands of one CH-column chunk of row m, fetched before the accumulator is read so
@@ -294,7 +308,7 @@ __device__ __forceinline__ void epi_apply(const GemmDev& p, int m, int img, int 
       *reinterpret_cast<uint4*>(dst) = pack8(v);
       continue;
     }
-    *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ld_out + ng) = pack8(v);
+    *reinterpret_cast<uint4*>(out_at(p, m, ng)) = pack8(v);
   }
 }
 
@@ -364,7 +378,7 @@ __device__ __forceinline__ void epi_apply_rows(const GemmDev& p, int m, int img,
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int mr = row0 + i;
-    if (mr < p.M) *reinterpret_cast<uint4*>(p.out + (size_t)mr * p.ld_out + n + 8 * (lane & 3)) = b[i];
+    if (mr < p.M) *reinterpret_cast<uint4*>(out_at(p, mr, n + 8 * (lane & 3))) = b[i];
   }
   (void)img;
 }
@@ -447,7 +461,7 @@ __device__ __forceinline__ void epi_plain_chunks(const GemmDev& p, uint32_t t_ro
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int mr = row0 + i;
-      if (mr < p.M) *reinterpret_cast<uint4*>(p.out + (size_t)mr * p.ld_out + n + 8 * (lane & 3)) = o[i];
+      if (mr < p.M) *reinterpret_cast<uint4*>(out_at(p, mr, n + 8 * (lane & 3))) = o[i];
     }
   }
 }
@@ -649,11 +663,13 @@ __global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
         const int m0 = m_blk * TM + (int)rank * BM;          // this CTA's A rows
         const int n0 = n_blk * BN + (int)rank * C::kBRows;   // this CTA's W rows
         int img0 = 0, y0 = 0;
-        if (p.taps == 9) {  // output geometry; the tensor map walks the input with stride cs
+        if (p.taps != 1) {  // output geometry; the tensor map walks the input with stride cs
           const int wo = p.W / p.cs, hwo = (p.H / p.cs) * wo;
           img0 = m0 / hwo;
           y0 = (m0 % hwo) / wo;
         }
+        // taps == 4: the output phase of this tile's columns (a tile never straddles two phases)
+        const int oph = p.taps == 4 ? (n_blk * BN) / p.up_co : 0;
         for (int kb = kb0; kb < kb1; kb += G, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
@@ -684,6 +700,8 @@ __global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
               if (p.taps == 9) {
                 const int dy = tap / 3 - 1, dx = tap % 3 - 1;
                 tma_load_4d_pair(dA, ma, fb, ch, dx, p.cs * y0 + dy, img0);
+              } else if (p.taps == 4) {  // 2x2 tap (ty, tx) of phase (py, px): input offset (ty + py - 1, tx + px - 1)
+                tma_load_4d_pair(dA, ma, fb, ch, (tap & 1) + (oph & 1) - 1, y0 + (tap >> 1) + (oph >> 1) - 1, img0);
               } else {
                 tma_load_2d_pair(dA, ma, fb, ch, m0);
               }
@@ -692,6 +710,8 @@ __global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
               if (p.taps == 9) {
                 const int dy = tap / 3 - 1, dx = tap % 3 - 1;
                 tma_load_4d(dA, ma, fb, ch, dx, p.cs * y0 + dy, img0);
+              } else if (p.taps == 4) {
+                tma_load_4d(dA, ma, fb, ch, (tap & 1) + (oph & 1) - 1, y0 + (tap >> 1) + (oph >> 1) - 1, img0);
               } else {
                 tma_load_2d(dA, ma, fb, ch, m0);
               }
@@ -1181,6 +1201,7 @@ TileChoice choose_tiles(const GemmArgs& a, bool allow_ws = true) {
   for (const TileCost& tcst : kTileCosts) {
     const int bn = tcst.bn;
     if (a.N % bn != 0 || (tcst.pair && !pair_ok)) continue;
+    if (a.taps == 4 && a.up_co % bn != 0) continue;  // upsample conv: a tile covers one output phase
     if (w8 && bn == 192) continue;                  // wo8 tiles: 64 / 128 / 160 / 256
     if (a.epi == kEpiGeglu && bn % 32) continue;  // whole 16 value + 16 gate row groups per tile
     const int tiles = (tcst.pair ? (a.M + 2 * BM - 1) / (2 * BM) : (a.M + BM - 1) / BM) * (a.N / bn);
@@ -1230,6 +1251,31 @@ GemmPlan gemm_plan(const GemmArgs& a, bool with_workspace) {
   return GemmPlan{t.bn, t.pair ? 1 : 0, t.splits, t.csplit};
 }
 
+void pack_upsample_conv_weights(const uint16_t* w3, int Co, int Ci, uint16_t* wp) {
+  // taps (ky or kx) of the 3x3 kernel that fold into 2x2 tap t of output phase q: R(q, t)
+  static const int kLo[2][2] = {{0, 1}, {0, 2}}, kHi[2][2] = {{0, 2}, {1, 2}};  // [q][t]: ky in [lo, hi]
+  for (int ph = 0; ph < 4; ++ph) {
+    const int py = ph >> 1, px = ph & 1;
+    for (int co = 0; co < Co; ++co)
+      for (int tap = 0; tap < 4; ++tap) {
+        const int ty = tap >> 1, tx = tap & 1;
+        uint16_t* dst = wp + ((size_t)(ph * Co + co) * 4 + tap) * Ci;
+        for (int ci = 0; ci < Ci; ++ci) {
+          const uint16_t* k3 = w3 + ((size_t)co * Ci + ci) * 9;
+          float acc = 0.f;
+          for (int ky = kLo[py][ty]; ky <= kHi[py][ty]; ++ky)
+            for (int kx = kLo[px][tx]; kx <= kHi[px][tx]; ++kx) {
+              __half_raw r;
+              r.x = k3[ky * 3 + kx];
+              acc += __half2float(__half(r));
+            }
+          const __half h = __float2half_rn(acc);
+          dst[ci] = static_cast<__half_raw>(h).x;
+        }
+      }
+  }
+}
+
 int gemm_launch_count(const GemmArgs& a) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK) return 1;
   const TileChoice t = choose_tiles(a);
@@ -1239,8 +1285,14 @@ int gemm_launch_count(const GemmArgs& a) {
 cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   const int cin = a.cin0 + a.cin1;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.K % BK != 0 || cin % BK != 0 || a.cin0 % BK != 0 ||
-      a.K != a.taps * cin || !(a.taps == 1 || a.taps == 9) || (a.w == nullptr && a.w8 == nullptr) || a.a0 == nullptr ||
-      (a.cin1 > 0 && a.a1 == nullptr))
+      a.K != a.taps * cin || !(a.taps == 1 || a.taps == 4 || a.taps == 9) || (a.w == nullptr && a.w8 == nullptr) ||
+      a.a0 == nullptr || (a.cin1 > 0 && a.a1 == nullptr))
+    return cudaErrorInvalidValue;
+  // upsample conv: fp16 weights, N = 4 phases x up_co (a multiple of 64, so every tile width the chooser
+  // may take -- 64 at least -- divides it), plain output [B, 2H, 2W, up_co]
+  if (a.taps == 4 && (a.up_co <= 0 || a.up_co % 64 != 0 || a.N != 4 * a.up_co || a.w8 != nullptr ||
+                      a.epi != kEpiPlain || a.residual != nullptr || a.rowbias != nullptr || a.out == nullptr ||
+                      (a.ld_out != 0 && a.ld_out != a.up_co) || a.bn != 0))
     return cudaErrorInvalidValue;
   if (a.epi != kEpiNchwF32 && a.epi != kEpiGeglu && a.N % 16 != 0) return cudaErrorInvalidValue;
   if ((a.epi == kEpiPlain || a.epi == kEpiHeads) && a.N > 16 && a.N % 32 != 0) return cudaErrorInvalidValue;
@@ -1258,11 +1310,14 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.M = a.M; d.N = a.N; d.K = a.K;
   d.taps = a.taps; d.cin0 = a.cin0; d.cin1 = a.cin1;
   d.H = a.H; d.W = a.W; d.cs = a.taps == 9 ? a.stride : 1;
+  d.up_w = a.taps == 4 ? a.W : 0;
+  d.up_co = a.taps == 4 ? a.up_co : 0;
   d.epi = a.epi; d.act = a.act;
   d.bias = a.bias; d.rowbias = a.rowbias; d.rowbias_ld = a.rowbias_ld;
   d.rows_per_image = a.rows_per_image > 0 ? a.rows_per_image : 1;
   d.residual = a.residual; d.ld_res = a.ld_res ? a.ld_res : a.N;
-  d.out = a.out; d.ld_out = a.ld_out ? a.ld_out : (a.epi == kEpiGeglu ? a.N / 2 : a.N);
+  d.out = a.out;
+  d.ld_out = a.taps == 4 ? a.up_co : (a.ld_out ? a.ld_out : (a.epi == kEpiGeglu ? a.N / 2 : a.N));
   d.out_f32 = a.out_f32;
   d.head_out0 = a.head_out[0]; d.head_out1 = a.head_out[1]; d.head_out2 = a.head_out[2];
   d.head_C = a.head_C; d.heads = a.heads; d.head_d = a.head_d; d.head_dp = a.head_dp;
@@ -1279,11 +1334,12 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   if (a.rowbias && a.rowbias_ld % 4) return cudaErrorInvalidValue;
 
   CUtensorMap ma0{}, ma1{}, mw{};
-  if (a.taps == 9) {
+  if (a.taps == 9 || a.taps == 4) {
     // Box over the input {64 channels, row, rows, images}, shifted per tap; with stride 2 the box spans
     // twice the output extent in x and y and TMA loads every second element (element strides 2), so
     // the tile still lands as 128 output pixels x 64 channels. Out-of-range rows / columns read zero.
-    const int st = a.stride;
+    // (taps == 4: the 2x2 phase convolutions walk the input like a stride-1 conv of its own size)
+    const int st = a.taps == 9 ? a.stride : 1;
     if (!(st == 1 || st == 2) || a.H % st || a.W % st) return cudaErrorInvalidValue;
     const int ho = a.H / st, wo = a.W / st, hw = a.H * a.W, hwo = ho * wo;
     int box_h, box_b;

@@ -31,6 +31,12 @@ struct GemmArgs {
   int lda0 = 0, lda1 = 0;      // row strides (elements) for taps == 1 (default cin)
   int B = 1, H = 1, W = 1;     // conv geometry (taps == 9): the INPUT image
   int stride = 1;              // taps == 9: 1, or 2 (output H/2 x W/2, pad 1; M = B * H/2 * W/2)
+  // taps == 4: nearest-2x upsample followed by a 3x3 pad-1 convolution, as four 2x2 convolutions of the
+  // low-resolution input (one per output phase (py, px)). H, W are the INPUT's; M = B * H * W rows (one
+  // per input pixel); N = 4 * up_co columns, phase-major (column ph * up_co + c is output channel c of
+  // phase ph = 2 py + px); w = [4 * up_co][4 taps][Cin] (pack_upsample_conv_weights); the output is NHWC
+  // [B, 2H, 2W, up_co]; bias [4 * up_co] (the conv bias repeated per phase).
+  int up_co = 0;
   const __half* w = nullptr;   // [N, K] K-major (conv: [Co][tap][Cin])
   const int8_t* w8 = nullptr;  // weight-only int8 alternative to w: [N, K] ...
   const float* wscale = nullptr;  // ... with per-row (output channel) scale [N]
@@ -69,6 +75,13 @@ struct GemmPlan {
   int bn, pair, splits, csplit;
 };
 GemmPlan gemm_plan(const GemmArgs& a, bool with_workspace);
+
+// Weights of the taps == 4 GEMM (nearest-2x upsample + 3x3 pad-1 conv as four 2x2 convolutions of the
+// low-resolution input) from a 3x3 kernel in the reference's layout w3[Co][Ci][3][3] (fp16 bits):
+// wp[(ph * Co + co) * 4 * Ci + (ty * 2 + tx) * Ci + ci], ph = 2 py + px, is the fp32 sum of the 3x3 taps
+// (ky, kx) with ky in R(py, ty), kx in R(px, tx), rounded once to fp16, where R(0,0) = {0},
+// R(0,1) = {1,2}, R(1,0) = {0,1}, R(1,1) = {2}: output row 2i + py reads input rows i + ty + py - 1.
+void pack_upsample_conv_weights(const uint16_t* w3, int Co, int Ci, uint16_t* wp);
 
 // GroupNorm(32) (+SiLU) over NHWC input that may be a channel concat of two
 // tensors. stats: groupnorm_scratch_bytes() bytes; receives (mean, rstd) per

@@ -252,6 +252,28 @@ def test_upsample_concat_add(sdg, cuda, gen):
     assert torch.equal(s, a + a)
 
 
+# ---------------------------------------------------------------- upsample block as one folded GEMM
+@pytest.mark.parametrize("B,C,H,W,ws", [
+    (2, 1280, 8, 8, False), (2, 1280, 16, 16, False), (2, 640, 32, 32, False),   # the UNet's three upsamplers
+    (2, 1280, 8, 8, True), (2, 1280, 16, 16, True),                              # with a split-K workspace
+    (1, 64, 1, 1, False), (4, 128, 2, 2, False), (1, 192, 4, 4, True), (3, 64, 16, 8, False),  # small / ragged
+])
+def test_upsample_conv3x3_matches_upsample_then_conv(sdg, cuda, gen, B, C, H, W, ws):
+    """vk_engine.cpp:693-697 (upsample_f32.comp nearest 2x, then the 3x3 pad-1 conv) against the
+    folded phase GEMM, which reads the H x W input directly."""
+    Co = C
+    x = rnd(B, C, H, W, g=gen).half()
+    w = rnd(Co, C, 3, 3, std=1 / math.sqrt(9 * C), g=gen).half()
+    b = rnd(Co, std=0.1, g=gen).float()
+    wp = torch.from_numpy(sdg.pack_upsample_conv_weight(w.cpu().numpy())).to(cuda)
+    work = torch.empty(32 * B * H * W * 4 * Co, dtype=torch.float32, device=cuda) if ws else None
+    y = sdg.upsample_conv3x3(nhwc(x), wp, b.repeat(4), workspace=work)
+    torch.cuda.synchronize()
+    ref = F.conv2d(R.upsample2x(x.float()), w.float(), b, padding=1)
+    assert y.shape == (B, 2 * H, 2 * W, Co)
+    assert rel(nchw(y), ref) < TOL
+
+
 # ---------------------------------------------------------------- split-K (deep levels: small M, large K)
 @pytest.mark.parametrize("M,N,K,resid", [(128, 1280, 11520, True), (512, 1280, 5120, False), (154, 640, 768, True),
                                          (300, 320, 2880, False)])
