@@ -65,6 +65,17 @@ def build_ops(sdg, dev):
         tag = "geglu" if act == 2 else ("linres" if res else "lin")
         ops[f"{tag}_{M}_{N}_{K}"] = (lambda xa=xa, wa=wa, ba=ba, ra=ra, ya=ya, act=act:
                                      sdg.linear(xa, wa, ba, residual=ra, act=act, out=ya), 2.0 * M * N * K, 0.0)
+    for C, H in ((1280, 8), (1280, 16), (640, 32)):                         # the upsample blocks (folded)
+        xu = rn(B, H, H, C)
+        wu = rn(4, C, 4, C, std=0.02)
+        bu = torch.zeros(4 * C, device=dev)
+        wsu = torch.empty(32 * B * H * H * 4 * C, dtype=torch.float32, device=dev)
+        yu = torch.empty((B, 2 * H, 2 * H, C), dtype=torch.float16, device=dev)
+        # FLOPs executed by the folded GEMM: 2 * (B H W) * (4 phases * C) * (4 taps * C), i.e. 16/36 of the direct
+        # count of a 3x3 conv on the 2H x 2H upsampled input
+        ops[f"upconv_{C}_{H}"] = (lambda xu=xu, wu=wu, bu=bu, yu=yu, wsu=wsu: sdg.upsample_conv3x3(xu, wu, bu, out=yu,
+                                                                                                   workspace=wsu),
+                                  2.0 * B * H * H * (4 * C) * (4 * C), 0.0)
     x = rn(B, 32, 32, 320)                                                  # config 1 conv1x1 skip
     w = rn(640, 320, std=0.02)
     y = torch.empty((B, 32, 32, 640), dtype=torch.float16, device=dev)
