@@ -31,11 +31,15 @@ namespace {
 
 // TPV: PV computed transposed, O^T[d][q] += V^T[d][keys] * P^T — one M=64 MMA per 16 keys covers
 // both query tiles (N = 256), half the PV instructions of the per-tile form (M=128, N=D16).
-template <int DP_, int BKV_, int NQT_, int D16_, bool ONES_, bool TPV_ = false>
+// POLY: of every 16 exponential pairs of a 32-key chunk, how many the softmax evaluates with ex2_poly
+// on the FMA pipe instead of ex2.approx.f16x2 on the MUFU pipe (balances the two pipes).
+template <int DP_, int BKV_, int NQT_, int D16_, bool ONES_, bool TPV_ = false, int POLY_ = 0>
 struct AttnCfg {
   static constexpr int DP = DP_, BKV = BKV_, NQT = NQT_, D16 = D16_;
   static constexpr bool ONES = ONES_;
   static constexpr bool TPV = TPV_;
+  static constexpr int POLY = POLY_;
+  static_assert(POLY >= 0 && POLY <= 16 && (POLY == 0 || 16 % POLY == 0), "POLY pairs spread evenly over 16");
   static_assert(!TPV || (NQT == 2 && BKV == 128 && ONES && D16 <= 64), "transposed PV: two 128-row query tiles");
   static constexpr int DV = TPV ? 64 : D16;                   // rows of a V^T atom
   static constexpr int NATOM = DP / 64;                       // 128B swizzle atoms along d
@@ -401,9 +405,14 @@ __global__ void __launch_bounds__(CF::kThreads, 1)
         const int q0c = (h & 1) * 4;
         uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2)  // exponent in fp16, 2^x two at a time (one MUFU op per pair)
-          pk[e >> 1] = ex2_f16x2(pack_half2(fmaf(__uint_as_float(c32[e]), p.sl2, -m_new),
-                                            fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new)));
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = fmaf(__uint_as_float(c32[e]), p.sl2, -m_new);
+          const float x1 = fmaf(__uint_as_float(c32[e + 1]), p.sl2, -m_new);
+          if (CF::POLY > 0 && (e >> 1) % (16 / (CF::POLY > 0 ? CF::POLY : 1)) == 0)
+            pk[e >> 1] = pack_half2(ex2_poly(x0), ex2_poly(x1));  // FMA pipe
+          else
+            pk[e >> 1] = ex2_f16x2(pack_half2(x0, x1));  // exponent in fp16, one MUFU op per pair
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 u = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
@@ -640,7 +649,10 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
   switch (a.d16) {
     case 48:
       if (small_q) return launch_cfg<AttnCfg<64, 64, 2, 48, true>>(a, err, s);
-      if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true, true>>(a, err, s);  // wide QK^T, transposed PV
+      // wide QK^T, transposed PV; every exponential on the MUFU pipe (POLY = 0): moving 2 / 4 / 8 of every
+      // 16 pairs to ex2_poly measured 130.2 -> 132.2 / 134.7 / 145.4 us at S = 4096 on B200 -- the softmax
+      // warps are bound by issue and dependent latency, not by the MUFU pipe
+      if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true, true>>(a, err, s);
       return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);  // short key sets (cross-attention)
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
     case 80: return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles

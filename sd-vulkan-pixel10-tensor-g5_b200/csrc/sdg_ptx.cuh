@@ -349,6 +349,20 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
+// 2^x on the FMA and integer pipes only (no MUFU), for softmax exponentials that would otherwise queue
+// behind the MUFU pipe. x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the low mantissa bits)
+// and f in [-0.5, 0.5]; 2^f by a cubic fitted for this kernel (minimax relative error 7.5e-5 on
+// [-0.5, 0.5], found by Lawson's iteratively reweighted least squares); 2^n is added to the exponent
+// field. x is clamped to >= -126 (below that the result is 0 after fp16 rounding anyway); x <= 127.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(0.0551716685f, f, 0.242611125f);
+  p = fmaf(p, f, 0.693260968f);
+  p = fmaf(p, f, 0.999928057f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
