@@ -65,7 +65,15 @@ struct ConvW {
   bool up = false;
 };
 struct ResW { Norm n1, n2; ConvW c1, c2; bool has_sc = false; Lin sc; int tp_off = 0, cin = 0, cout = 0; };
-struct TfW { Norm gn, ln1, ln2, ln3; Lin pin, qkv, out1, q2, kv2, out2, ff1, ff2, pout; int C = 0; };
+// ln_folded (fp16 engine): the gammas / betas of LayerNorms 1 and 2 live in the weights of the GEMMs that
+// read the normalised rows (qkv after ln1, q2 after ln2: w * gamma, bias + w beta), and cs1 / cs2 hold each
+// folded row's sum for the epilogue rstd * (acc - mean * colsum) + bias. LayerNorm 3 (before the GEGLU
+// FF-proj) stays a launch: its epilogue taking the fold measured slower than the launch it saves.
+struct TfW {
+  Norm gn, ln1, ln2, ln3; Lin pin, qkv, out1, q2, kv2, out2, ff1, ff2, pout; int C = 0;
+  bool ln_folded = false;
+  float* cs1 = nullptr; float* cs2 = nullptr;
+};
 struct UNetW {
   Lin t1, t2;
   ConvW conv_in, conv_out;
@@ -78,6 +86,8 @@ struct UNetW {
   ResW up_res[4][3];
   TfW up_tf[4][3];  // [0][*] unused
   ConvW up_us[3];
+  float* ln_one = nullptr;   // [1280] ones / zeros: the affine of a normalise-only LayerNorm launch
+  float* ln_zero = nullptr;
   __half* tp_w = nullptr;
   int8_t* tp_w8 = nullptr;
   float* tp_ws = nullptr;
@@ -349,13 +359,59 @@ struct WeightPacker {
     for (int o = 0; o < out; ++o)
       for (int i = 0; i < in; ++i) d[(size_t)(row0 + o) * ld + i] = hw ? hw->data[(size_t)i * out + o] : 0;
   }
-  void linear(Lin& L, const std::string& pf, int in, int out, bool bias) {
+  // returns the offset of the packed [out][in] matrix in the arena image
+  size_t linear(Lin& L, const std::string& pf, int in, int out, bool bias, size_t* bias_off = nullptr) {
     L.N = out; L.K = in;
     size_t o = reserve((size_t)in * out * 2);
     place(&L.w, o);
     mat(o, out, in, &L.w, &L.w8, &L.ws);
     linear_rows(o, 0, in, pf + ".weight", in, out);
-    if (bias) vecf(&L.b, pf + ".bias", out);
+    if (bias) {
+      if (bias_off) *bias_off = (off + 255) & ~size_t(255);  // where vecf places it
+      vecf(&L.b, pf + ".bias", out);
+    }
+    return o;
+  }
+  // LayerNorm `ln` ([K] gamma, beta) folded into the GEMM that reads its output (fp16 engine): the packed
+  // [N][K] matrix at w_off becomes fp16(w * gamma) (per input column), the bias (at *bias_off, or a new
+  // array placed into *bias_slot) gains sum_k w[n][k] beta[k] (unfolded w, fp32), and a new [N] array
+  // placed into *cs_slot holds sum_k of the folded fp16 row -- so W (gamma * (x - mean) * rstd + beta) + b
+  // = rstd * (W' x - mean * cs) + b'.
+  void fold_ln(size_t w_off, int N, int K, const std::string& ln, const size_t* bias_off, float** bias_slot,
+               float** cs_slot) {
+    const HostWeight* g = get(ln + ".weight", K);
+    const HostWeight* be = get(ln + ".bias", K);
+    size_t bo = 0;
+    if (bias_off) {
+      bo = *bias_off;
+    } else {
+      bo = reserve((size_t)N * 4);
+      place(bias_slot, bo);
+      std::memset(staging.data() + bo, 0, (size_t)N * 4);
+    }
+    const size_t co = reserve((size_t)N * 4);
+    place(cs_slot, co);
+    uint16_t* w = reinterpret_cast<uint16_t*>(staging.data() + w_off);  // (after the last reserve)
+    float* bias = reinterpret_cast<float*>(staging.data() + bo);
+    float* cs = reinterpret_cast<float*>(staging.data() + co);
+    std::vector<float> gf(K, 1.f), bf(K, 0.f);
+    for (int k = 0; k < K; ++k) {
+      if (g) gf[k] = h2f(g->data[k]);
+      if (be) bf[k] = h2f(be->data[k]);
+    }
+    for (int n = 0; n < N; ++n) {
+      uint16_t* row = w + (size_t)n * K;
+      double add = 0.0, sum = 0.0;
+      for (int k = 0; k < K; ++k) {
+        const float wk = h2f(row[k]);
+        add += (double)wk * bf[k];
+        const __half h = __float2half_rn(wk * gf[k]);
+        row[k] = static_cast<__half_raw>(h).x;
+        sum += (double)__half2float(h);
+      }
+      bias[n] += (float)add;
+      cs[n] = (float)sum;
+    }
   }
   // conv [Co,Ci,k,k] -> [Co][k*k][Ci] (1x1: [Co][Ci])
   void conv(ConvW& c, const std::string& pf, int ci, int co, int k) {
@@ -447,6 +503,7 @@ int Engine::prepare() {
     P.norm(t.ln1, b + ".norm1", C);
     P.norm(t.ln2, b + ".norm2", C);
     P.norm(t.ln3, b + ".norm3", C);
+    t.ln_folded = !wo8;  // (the int8 scheme quantises the unfolded weights, as the reference's does)
     {  // fused QKV [3C][C]
       t.qkv.N = 3 * C; t.qkv.K = C;
       size_t o = P.reserve((size_t)3 * C * C * 2);
@@ -455,9 +512,13 @@ int Engine::prepare() {
       P.linear_rows(o, 0, C, b + ".attn1.to_q.weight", C, C);
       P.linear_rows(o, C, C, b + ".attn1.to_k.weight", C, C);
       P.linear_rows(o, 2 * C, C, b + ".attn1.to_v.weight", C, C);
+      if (t.ln_folded) P.fold_ln(o, 3 * C, C, b + ".norm1", nullptr, &t.qkv.b, &t.cs1);
     }
     P.linear(t.out1, b + ".attn1.to_out.0", C, C, true);
-    P.linear(t.q2, b + ".attn2.to_q", C, C, false);
+    {
+      const size_t o = P.linear(t.q2, b + ".attn2.to_q", C, C, false);
+      if (t.ln_folded) P.fold_ln(o, C, C, b + ".norm2", nullptr, &t.q2.b, &t.cs2);
+    }
     {  // fused cross K/V [2C][768]
       t.kv2.N = 2 * C; t.kv2.K = kCtxDim;
       size_t o = P.reserve((size_t)2 * C * kCtxDim * 2);
@@ -536,6 +597,14 @@ int Engine::prepare() {
           P.conv_upsample(w.up_us[i], pf, up_out[i], up_out[i]);
       }
     }
+  }
+  {  // affine of the normalise-only LayerNorm launches (folded LayerNorms whose GEMMs split K)
+    const size_t o1 = P.reserve(1280 * 4), o0 = P.reserve(1280 * 4);
+    P.place(&w.ln_one, o1);
+    P.place(&w.ln_zero, o0);
+    float* f1 = reinterpret_cast<float*>(P.staging.data() + o1);
+    float* f0 = reinterpret_cast<float*>(P.staging.data() + o0);
+    for (int i = 0; i < 1280; ++i) { f1[i] = 1.f; f0[i] = 0.f; }
   }
   P.norm(w.norm_out, "conv_norm_out", 320);
   P.conv(w.conv_out, "conv_out", 320, 4, 3);
@@ -752,28 +821,61 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
   __half* hn = alloc_h((size_t)M * C);
   __half* o = alloc_h((size_t)M * C);
   __half* gg = alloc_h((size_t)M * 4 * C);
-  auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
+  auto lin_args = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
     GemmArgs a;
     a.M = M; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b; a.residual = resid;
     a.out = y;
-    gemm(a, kCatGemm);
+    return a;
   };
-  auto ln = [&](const __half* xin, const Norm& n) {
+  auto lin = [&](const __half* A, int K, const Lin& L, const __half* resid, __half* y) {
+    gemm(lin_args(A, K, L, resid, y), kCatGemm);
+  };
+  auto ln = [&](const __half* xin, const float* g, const float* b) {
     cat_bytes[kCatLN] += 2.0 * 2.0 * M * C;
     if (dry_ || !ok()) { launches_++; return; }
-    issue(kCatLN, "layernorm", 1, [=, g = n.g, b = n.b](cudaStream_t s) {
+    issue(kCatLN, "layernorm", 1, [=](cudaStream_t s) {
       return launch_layernorm(xin, M, C, g, b, kLnEps, hn, s);
     }, "layernorm M=" + std::to_string(M) + " C=" + std::to_string(C), 0.0, 2.0 * 2.0 * M * C);
   };
-  auto heads = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1, __half* o2,
-                   int vt_idx, int spad) {
+  auto heads_args = [&](const __half* A, int Mr, int K, const Lin& L, int rows_per_image, __half* o0, __half* o1,
+                        __half* o2, int vt_idx, int spad) {
     GemmArgs a;
     a.M = Mr; a.N = L.N; a.K = K; a.a0 = A; a.cin0 = K; set_w(a, L.w, L.w8, L.ws); a.bias = L.b;
     a.epi = kEpiHeads; a.rows_per_image = rows_per_image;
     a.head_out[0] = o0; a.head_out[1] = o1; a.head_out[2] = o2;
     a.head_C = C; a.heads = kHeads; a.head_d = d; a.head_dp = dp;
     a.head_vt = vt_idx; a.head_d16 = d16; a.head_spad = spad;
-    gemm(a, kCatGemm);
+    return a;
+  };
+  // A GEMM that writes the residual stream tt (prod) followed by a LayerNorm of tt feeding `cons`.
+  // colsum non-null: the LayerNorm's affine is folded into cons's weights (fp16 engine, LayerNorms 1 and
+  // 2). If both GEMMs then run single-pass 1-CTA plans, prod's epilogue writes per-row partial sums and
+  // cons reads tt itself and normalises in its epilogue -- no LayerNorm launch, no hn round trip;
+  // otherwise a normalise-only LayerNorm launch writes hn. colsum null: a LayerNorm launch with the
+  // affine. Replaces vk_engine.cpp:652/658/666 (layernorm) + the matmul that follows.
+  auto ln_then = [&](GemmArgs prod, const Norm& n, const float* colsum, GemmArgs cons) {
+    auto single = [&](const GemmArgs& a) {
+      const GemmPlan pl = gemm_plan(a, !on_side_);
+      return pl.splits == 1 && pl.csplit == 1 && !pl.pair && pl.bn >= 32 && a.N % pl.bn == 0;
+    };
+    const bool fold = colsum != nullptr && single(prod) && single(cons);
+    if (fold) {
+      const int parts = 2 * (prod.N / gemm_plan(prod, !on_side_).bn);
+      float2* st = reinterpret_cast<float2*>(alloc_f((size_t)M * parts * 2));
+      prod.ln_stat_out = st; prod.ln_stat_ld = parts;
+      cons.a0 = prod.out;
+      cons.ln_stat_in = st; cons.ln_stat_parts = parts; cons.ln_C = C; cons.ln_eps = kLnEps; cons.ln_colsum = colsum;
+      gemm(prod, kCatGemm);
+      gemm(cons, kCatGemm);
+      return;
+    }
+    gemm(prod, kCatGemm);
+    if (colsum)  // the affine lives in cons's weights: normalise only
+      ln(prod.out, e_.w.ln_one, e_.w.ln_zero);
+    else
+      ln(prod.out, n.g, n.b);
+    cons.a0 = hn;
+    gemm(cons, kCatGemm);
   };
   auto attn = [&](const __half* q, const __half* k, const __half* vt, int Sk, int vt_ld) {
     cat_flops[kCatAttn] += 4.0 * B * kHeads * (double)S * Sk * d;
@@ -786,14 +888,12 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
               " d=" + std::to_string(d),
           4.0 * B * kHeads * (double)S * Sk * d);
   };
-  lin(g, C, t.pin, nullptr, tt);                                   // proj_in (1x1)
-  ln(tt, t.ln1);
   const int spad = (S + 7) / 8 * 8;                                // V^T rows are 16-byte multiples
-  heads(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, spad);         // Q, K, V^T
+  ln_then(lin_args(g, C, t.pin, nullptr, tt), t.ln1, t.cs1,        // proj_in (1x1), LayerNorm 1,
+          heads_args(hn, M, C, t.qkv, S, ab.q, ab.k, ab.vt, 2, spad));  // Q, K, V^T
   attn(ab.q, ab.k, ab.vt, S, spad);                                // self-attention
-  lin(o, C, t.out1, tt, tt);                                       // t += to_out(attn)
-  ln(tt, t.ln2);
-  heads(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0);         // Q (cross)
+  ln_then(lin_args(o, C, t.out1, tt, tt), t.ln2, t.cs2,            // t += to_out(attn), LayerNorm 2,
+          heads_args(hn, M, C, t.q2, S, ab.q, nullptr, nullptr, -1, 0));  // Q (cross)
   if (!ctx_cached) {  // K, V^T from the context: issued on the side stream at the start of the forward
     if (ci < (int)kv_ready_.size())
       join(kv_ready_[ci]);
@@ -801,13 +901,11 @@ Buf Builder::transformer(const TfW& t, const Buf& x, int H, int W) {
       ctx_kv(t, cb);
   }
   attn(ab.q, cb.k, cb.vt, kCtxLen, kCtxPad);                       // cross-attention
-  lin(o, C, t.out2, tt, tt);
-  ln(tt, t.ln3);
   {
-    GemmArgs a;
+    GemmArgs a;                                                    // GEGLU FF-proj
     a.M = M; a.N = t.ff1.N; a.K = C; a.a0 = hn; a.cin0 = C; set_w(a, t.ff1.w, t.ff1.w8, t.ff1.ws); a.bias = t.ff1.b;
     a.epi = kEpiGeglu; a.out = gg; a.ld_out = 4 * C;
-    gemm(a, kCatGemm);
+    ln_then(lin_args(o, C, t.out2, tt, tt), t.ln3, nullptr, a);    // t += to_out(cross-attn), LayerNorm 3
   }
   lin(gg, 4 * C, t.ff2, tt, tt);                                   // t += ff(t)
   lin(tt, C, t.pout, x.p, out.p);                                  // proj_out + x

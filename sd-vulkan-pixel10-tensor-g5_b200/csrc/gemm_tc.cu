@@ -78,6 +78,17 @@ struct GemmDev {
   float* ws;                 // [splits][M][N] fp32 partials when splits > 1
   const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
+  // LayerNorm folded into the GEMMs around it. Producer (plain single-pass epilogue): per output row,
+  // the (sum, sum of squares) of this tile's columns goes to stat_out[m * stat_ld + n_blk]. Consumer
+  // (attention-head or GEGLU epilogue): A is the raw row x, W already carries gamma; per row
+  // mean / rstd come from the stat_parts partials at stat_in[m * stat_parts ..], and the epilogue
+  // computes rstd * (acc - mean * colsum[n]) + bias[n] (bias = b + W beta).
+  float2* stat_out;
+  int stat_ld;
+  const float2* stat_in;
+  int stat_parts;
+  float ln_inv_c, ln_eps;
+  const float* colsum;
   int stall_it;              // failure-path test: k-block iteration whose stage is never loaded (-1: none)
   unsigned long long wait_ns;  // limit of every bounded wait
 };
@@ -388,9 +399,9 @@ __device__ __forceinline__ void epi_apply_rows(const GemmDev& p, int m, int img,
 // straight-line code without per-group branches on the launch arguments. res_next holds the
 // first chunk's residual on entry (loaded before the accumulator wait). Same arithmetic, order of
 // operations and stores as epi_apply_rows.
-template <int BN, int kSplit, bool W8, bool RES, bool ROWB, bool SILU>
+template <int BN, int kSplit, bool W8, bool RES, bool ROWB, bool SILU, bool STATS = false>
 __device__ __forceinline__ void epi_plain_chunks(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
-                                                 int eh, int lane, uint4 (&res_next)[4]) {
+                                                 int eh, int lane, uint4 (&res_next)[4], float& s1, float& s2) {
   const int im = mvalid ? img : 0;  // rows past M (last partial tile) must not index past the last image
   const float* rb_row = ROWB ? p.rowbias + (size_t)im * p.rowbias_ld : nullptr;
   const __half* res_row = RES ? p.residual + (size_t)m * p.ld_res : nullptr;
@@ -455,6 +466,13 @@ __device__ __forceinline__ void epi_plain_chunks(const GemmDev& p, uint32_t t_ro
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = silu_f(v[j]);
       }
+      if constexpr (STATS) {  // LayerNorm partials of this row (fp32 values before the fp16 rounding)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s1 += v[j];
+          s2 = fmaf(v[j], v[j], s2);
+        }
+      }
       o[g] = pack8(v);
     }
     quad_transpose(o, lane);
@@ -468,30 +486,60 @@ __device__ __forceinline__ void epi_plain_chunks(const GemmDev& p, uint32_t t_ro
 
 template <int BN, int kSplit, bool W8>
 __device__ __forceinline__ void epi_plain_dispatch(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
-                                                   int eh, int lane, uint4 (&res_next)[4]) {
-  const int sel = (p.residual ? 1 : 0) | (p.rowbias ? 2 : 0) | (p.act == 1 ? 4 : 0);
+                                                   int eh, int lane, uint4 (&res_next)[4], float& s1, float& s2) {
+  // (LayerNorm statistics come only with a plain output: no row bias, no activation; checked on the host)
+  const int sel = (p.residual ? 1 : 0) | (p.rowbias ? 2 : 0) | (p.act == 1 ? 4 : 0) | (p.stat_out ? 8 : 0);
   switch (sel) {
-    case 0: epi_plain_chunks<BN, kSplit, W8, false, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 1: epi_plain_chunks<BN, kSplit, W8, true, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 2: epi_plain_chunks<BN, kSplit, W8, false, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 3: epi_plain_chunks<BN, kSplit, W8, true, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 4: epi_plain_chunks<BN, kSplit, W8, false, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 5: epi_plain_chunks<BN, kSplit, W8, true, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    case 6: epi_plain_chunks<BN, kSplit, W8, false, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
-    default: epi_plain_chunks<BN, kSplit, W8, true, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next); break;
+    case 0: epi_plain_chunks<BN, kSplit, W8, false, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 1: epi_plain_chunks<BN, kSplit, W8, true, false, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 2: epi_plain_chunks<BN, kSplit, W8, false, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 3: epi_plain_chunks<BN, kSplit, W8, true, true, false>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 4: epi_plain_chunks<BN, kSplit, W8, false, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 5: epi_plain_chunks<BN, kSplit, W8, true, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 6: epi_plain_chunks<BN, kSplit, W8, false, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    case 7: epi_plain_chunks<BN, kSplit, W8, true, true, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2); break;
+    default:  // the statistics variants exist for fp16 weights only (the wo8 engine keeps its LayerNorm launches)
+      if constexpr (!W8) {
+        if (sel == 8)
+          epi_plain_chunks<BN, kSplit, W8, false, false, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2);
+        else
+          epi_plain_chunks<BN, kSplit, W8, true, false, false, true>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2);
+      }
+      break;
   }
+}
+
+// Per-row LayerNorm factors of a consumer GEMM tile row m: rstd and rstd * mean from the producer's
+// stat_parts (sum, sum of squares) partials (an even count, 16-byte aligned rows), summed in order
+// (deterministic); var = E[x^2] - mean^2.
+__device__ __forceinline__ void ln_row_factors(const GemmDev& p, int m, bool mvalid, float& rstd, float& mr) {
+  float s1 = 0.f, s2 = 0.f;
+  if (mvalid) {
+    const float4* src = reinterpret_cast<const float4*>(p.stat_in + (size_t)m * p.stat_parts);
+#pragma unroll 4
+    for (int i = 0; i < p.stat_parts / 2; ++i) {
+      const float4 v = __ldg(src + i);
+      s1 += v.x + v.z;
+      s2 += v.y + v.w;
+    }
+  }
+  const float mean = s1 * p.ln_inv_c;
+  const float var = fmaxf(fmaf(s2, p.ln_inv_c, -mean * mean), 0.f);
+  rstd = rsqrtf(var + p.ln_eps);
+  mr = rstd * mean;
 }
 
 // Attention-head epilogue (Q / K / V projections: bias, no residual, no activation) of a warp's
 // 32-column chunks: scatter into the padded per-head layouts, V (head_vt) transposed.
-template <int BN, int kSplit, bool W8>
+template <int BN, int kSplit, bool W8, bool LN = false>
 __device__ __forceinline__ void epi_heads_chunks(const GemmDev& p, uint32_t t_row, int m, int img, int n0, bool mvalid,
-                                                 int eh) {
+                                                 int eh, float rstd = 1.f, float mr = 0.f) {
   const int s_idx = m - img * p.rows_per_image;
 #pragma unroll 1
   for (int c = eh * 32; c < BN; c += kSplit * 32) {
     const int n = n0 + c;
     if (p.bias && n + kSplit * 32 < p.N) prefetch_l1(p.bias + n + kSplit * 32);
+    if (LN && n + kSplit * 32 < p.N) prefetch_l1(p.colsum + n + kSplit * 32);
     uint32_t r[32];
     tmem_ld32(t_row + c, r);
     float4 b[8];
@@ -499,6 +547,12 @@ __device__ __forceinline__ void epi_heads_chunks(const GemmDev& p, uint32_t t_ro
     for (int q = 0; q < 8; ++q)
       b[q] = (p.bias && n + 4 * q < p.N) ? __ldg(reinterpret_cast<const float4*>(p.bias + n) + q)
                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 cs[LN ? 8 : 1];
+    if constexpr (LN) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        cs[q] = n + 4 * q < p.N ? __ldg(reinterpret_cast<const float4*>(p.colsum + n) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     tmem_wait_ld();
     if (!mvalid || n >= p.N) continue;
 #pragma unroll
@@ -511,6 +565,11 @@ __device__ __forceinline__ void epi_heads_chunks(const GemmDev& p, uint32_t t_ro
       if constexpr (W8) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] *= __ldg(p.wscale + ng + j);
+      }
+      if constexpr (LN) {  // LayerNorm of the A row, folded: rstd * acc - rstd * mean * colsum
+        const float* c8 = reinterpret_cast<const float*>(&cs[2 * g]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = fmaf(rstd, v[j], -mr * c8[j]);
       }
       const float4 b0 = b[2 * g], b1 = b[2 * g + 1];
       v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
@@ -843,6 +902,10 @@ __global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
       uint4 res_next[C::kChunk / 8];
       const bool fused_res = csp == 1 && p.splits == 1 && p.epi != kEpiNchwF32 && p.epi != kEpiGeglu && p.residual;
       if (fused_res) res_load<C::kChunk>(p, m, n0 + eh * C::kChunk, mvalid, res_next);
+      // LayerNorm consumer (attention-head epilogue): the row's factors, read while the main loop runs
+      float ln_rstd = 1.f, ln_mr = 0.f;
+      const bool ln_in = EK == kEkHeads && p.stat_in != nullptr;
+      if (ln_in) ln_row_factors(p, m, mvalid, ln_rstd, ln_mr);
       bool ok = mbar_wait(tfull_bar(acc), acc_ph, p.err, kDevTimeoutAcc, p.wait_ns);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -850,9 +913,16 @@ __global__ void __launch_bounds__(gemm_threads(W8, EK), 1)
       constexpr int CH = C::kChunk;
       if constexpr (EK != kEkGeneric) static_assert(CH == 32, "the specialised epilogues walk 32-column chunks");
       if constexpr (EK == kEkPlain) {
-        epi_plain_dispatch<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh, lane, res_next);
+        float s1 = 0.f, s2 = 0.f;
+        epi_plain_dispatch<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh, lane, res_next, s1, s2);
+        // LayerNorm producer: each epilogue warp's partial over its column chunks of the row (the kSplit
+        // warps of a lane quadrant hold disjoint chunks; no barrier between them)
+        if (p.stat_out && mvalid) p.stat_out[(size_t)m * p.stat_ld + n_blk * kSplit + eh] = make_float2(s1, s2);
       } else if constexpr (EK == kEkHeads) {
-        epi_heads_chunks<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh);
+        if (ln_in)
+          epi_heads_chunks<BN, kSplit, W8, true>(p, t_row, m, img, n0, mvalid, eh, ln_rstd, ln_mr);
+        else
+          epi_heads_chunks<BN, kSplit, W8>(p, t_row, m, img, n0, mvalid, eh);
       } else if (csp > 1) {
         // cluster K split: the partial tile stays in TMEM until every CTA of the cluster is
         // past its main loop (reduction below)
@@ -1326,6 +1396,21 @@ cudaError_t launch_gemm(const GemmArgs& a, int* dev_err, cudaStream_t s) {
   d.csplit = tc.csplit;
   d.wscale = a.w8 ? a.wscale : nullptr;
   d.err = dev_err;
+  d.stat_out = a.ln_stat_out; d.stat_ld = a.ln_stat_ld;
+  d.stat_in = a.ln_stat_in; d.stat_parts = a.ln_stat_parts;
+  d.ln_inv_c = a.ln_C > 0 ? 1.f / (float)a.ln_C : 0.f; d.ln_eps = a.ln_eps;
+  d.colsum = a.ln_colsum;
+  if (a.ln_stat_out || a.ln_stat_in) {  // LayerNorm folding: single-pass 1-CTA fp16 plans only
+    const bool single = tc.splits == 1 && tc.csplit == 1 && !tc.pair && bn >= 32 && a.w8 == nullptr;
+    if (!single) return cudaErrorInvalidValue;
+    if (a.ln_stat_out && (a.epi != kEpiPlain || a.rowbias || a.act != 0 || a.N % bn || a.ln_stat_ld < 2 * (a.N / bn) ||
+                          a.taps == 4))
+      return cudaErrorInvalidValue;
+    if (a.ln_stat_in && (!(a.epi == kEpiHeads && !a.residual && a.act == 0) || a.ln_stat_parts <= 0 ||
+         a.ln_stat_parts % 2 || a.ln_C <= 0 || !a.ln_colsum ||
+         ((reinterpret_cast<uintptr_t>(a.ln_colsum) | reinterpret_cast<uintptr_t>(a.ln_stat_in)) & 15)))
+      return cudaErrorInvalidValue;
+  }
   d.stall_it = a.test_stall_iter;
   d.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kWaitTimeoutNs;
   if (a.w8 && !a.wscale) return cudaErrorInvalidValue;

@@ -59,6 +59,20 @@ struct GemmArgs {
   int bn = 0;                       // tile N (0 = choose)
   float* ws = nullptr;              // split-K workspace (fp32); split-K only when large enough
   size_t ws_bytes = 0;
+  // LayerNorm folded into the neighbouring GEMMs (single-pass 1-CTA fp16 plans only; launch_gemm refuses
+  // other plans). Producer (plain output, no row bias, no activation): per output row, one (sum, sum of
+  // squares) partial per epilogue warp and tile column block at ln_stat_out[m * ln_stat_ld + 2 * n_blk + w],
+  // ln_stat_ld = 2 * N / tile width. Consumer (attention-head epilogue): A = the raw rows, w with
+  // gamma folded in (w * gamma per input column), bias = b + w beta, ln_colsum[n] = sum_k of the folded fp16
+  // w row; the epilogue applies rstd * (acc - mean * colsum) + bias with mean / rstd over ln_C columns
+  // from the ln_stat_parts partials of each row.
+  float2* ln_stat_out = nullptr;
+  int ln_stat_ld = 0;
+  const float2* ln_stat_in = nullptr;
+  int ln_stat_parts = 0;
+  int ln_C = 0;
+  float ln_eps = 0.f;
+  const float* ln_colsum = nullptr;
   // Failure-path test only (sdg_selftest_stalled_gemm): the producer leaves the pipeline stage of this
   // k-block iteration (counted per CTA) unloaded, so the waits on it expire after wait_limit_ns.
   int test_stall_iter = -1;
