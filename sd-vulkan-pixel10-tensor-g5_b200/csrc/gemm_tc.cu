@@ -42,7 +42,10 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kMaxCsplitCtas = 8;  // cluster K split: at most the portable cluster size
+// cluster K split: up to 10 CTAs (a non-portable cluster size above 8). Measured on B200 for the 8x8-level
+// 128 x 1280 x 11520 conv: 16.4 us with a 14-way workspace split, 14.35 / 13.9 / 13.5 us over clusters of
+// 8 / 9 / 10 CTAs, 24 us and more over clusters of 12 to 16 (too few of them co-resident)
+constexpr int kMaxCsplitCtas = 10;
 // epilogue kinds of the kernel instantiations (gemm_tc_kernel's EK)
 constexpr int kEkGeneric = 0, kEkPlain = 1, kEkHeads = 3;
 // Epilogue warps: two per TMEM lane quadrant (10 warps in all: at most three per SM sub-partition,
@@ -1141,6 +1144,10 @@ cudaError_t set_gemm_smem() {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, EK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN, W8, PAIR>::kSmem);
     if (e != cudaSuccess) return e;
+    if (EK == kEkGeneric && !PAIR) {  // cluster K splits of up to 16 CTAs
+      e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, EK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+    }
     attr_set[dev] = true;
   }
   return cudaSuccess;
@@ -1192,7 +1199,9 @@ struct TileChoice {
 
 // Cost model, fitted to launch times measured on B200 over the SD1.5 UNet's GEMM and conv shapes
 // (graph replay, 1-CTA and CTA-pair tiles of width 64..256, 1..32 K splits; median error 5 %):
-//   t = waves * (k-blocks per unit * t_kb + t_unit) + (splits > 1 ? 5.5 us + 0.181 us per MB of partials : 0)
+//   t = waves * (k-blocks per unit * t_kb + t_unit) + (splits > 1 ? 8.5 us + 0.181 us per MB of partials : 0)
+// (the workspace-split constant was refitted from 5.5 us: the forward's three workspace-split shapes,
+// 128 x 1280 x 11520 / 23040 and 512 x 1280 x 23040 on CTA pairs, measured 3.0-3.2 us above the model)
 // Tiles whose stages hold two k-blocks (1-CTA widths <= 160, every CTA-pair width) cost ~0.26-0.29 us
 // per 64-deep k-block and CTA; the 1-CTA 192/256 tiles, one k-block per stage, 0.33-0.38. t_unit
 // (pipeline fill + epilogue) grows with the tile width.
@@ -1229,7 +1238,8 @@ int cluster_capacity(int cs) {
     using C = Cfg<160, false, false>;
     auto k = gemm_tc_kernel<160, false, false, kEkGeneric>;
     int n = 0;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem) == cudaSuccess) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem) == cudaSuccess &&
+        cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(cs * 64);
       cfg.blockDim = dim3(C::kThreads);
@@ -1283,14 +1293,16 @@ TileChoice choose_tiles(const GemmArgs& a, bool allow_ws = true) {
       if (real_sp != sp) continue;
       if (sp > 1 && allow_ws) {  // workspace split-K + reduce launch
         const int waves = (tiles * sp + teams - 1) / teams;
-        const double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit) + 5.5 +
+        const double t = waves * (kbs * tcst.us_per_kb + tcst.us_per_unit) + 8.5 +
                          0.181 * ((double)sp * a.M * a.N * 4.0 / 1e6);
         if (t < best_t) {
           best_t = t;
           best = TileChoice{bn, sp, kbs, tcst.pair, 1};
         }
       }
-      if (sp == 1 || (!tcst.pair && sp <= kMaxCsplitCtas)) {  // single pass, or cluster split-K
+      // single pass, or cluster split-K (not on 1-CTA 256-wide tiles: measured 1.8x slower than the
+      // workspace split of the 512 x 1280 x 23040 conv and never the fastest plan of a UNet shape)
+      if (sp == 1 || (!tcst.pair && bn != 256 && sp <= kMaxCsplitCtas)) {
         const int cap = sp > 1 ? cluster_capacity(sp) : teams;  // resident clusters (sp > 1) or CTAs
         if (cap <= 0) continue;                                  // no cluster of this size fits
         const int waves = (tiles + cap - 1) / cap;

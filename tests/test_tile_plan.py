@@ -6,8 +6,9 @@ resident clusters; with one it asks the device how many clusters of each size fi
 one a B200 runs. The invariants below hold either way.
 
 Invariants the kernels rely on: the tile width divides N (or is the ragged 64 fallback), a K split
-is either a workspace split or a cluster split of at most 8 CTAs (never both, never on a CTA pair),
-every split owns at least one 64-deep k-block, and without a workspace no workspace split is chosen.
+is either a workspace split or a cluster split of at most 10 CTAs (never both, never on a CTA pair or a
+256-wide 1-CTA tile), every split owns at least one 64-deep k-block, and without a workspace no workspace
+split is chosen.
 """
 import pytest
 
@@ -28,9 +29,10 @@ def test_plan_invariants(sdg, M, N, K, with_ws):
     bn, pair, splits, csplit = pl["bn"], pl["pair"], pl["splits"], pl["csplit"]
     assert bn in (16, 64, 128, 160, 192, 256)
     assert N % bn == 0 or bn == 64
-    assert splits >= 1 and 1 <= csplit <= 8
+    assert splits >= 1 and 1 <= csplit <= 10
     assert not (splits > 1 and csplit > 1)
     assert not (pair and csplit > 1)
+    assert not (bn == 256 and csplit > 1)
     if not with_ws:
         assert splits == 1
     kb = K // 64
