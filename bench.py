@@ -35,10 +35,10 @@ METRIC = "UNet fwd/s (B=2 CFG, 64×64 latent) at 1/2/4/8 B200; % dense-fp16 tens
 UNIT = "fwd/s"
 B, H, W = 2, 64, 64
 FLOPS_PER_FWD = 1.606e12          # algorithmic FLOPs per B=2 64x64 forward (direct-conv count)
-# DRAM bytes (read + write) per gemm_tc_kernel launch, averaged over the 210 GEMM launches (and 17 split-K
+# DRAM bytes (read + write) per gemm_tc_kernel launch, averaged over the 210 GEMM launches (and 3 split-K
 # reduce launches) of one B=2 64x64 forward, from a one-pass ncu launch list of this bench
-# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/forward_launches_b2_64x64.md): 2.85 GB per forward
-GEMM_TRAFFIC_PER_LAUNCH = 13.56e6
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/forward_launches_b2_64x64.md): 2.73 GB per forward
+GEMM_TRAFFIC_PER_LAUNCH = 12.98e6
 GEMM_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of every GEMM launch of one forward "
                      "(split-K reduce launches included) / 210 GEMM launches; serialised replay, cold caches")
 L2_FLUSH_BYTES = 256 << 20        # > 126 MB L2
