@@ -655,7 +655,9 @@ cudaError_t launch_attention(const AttnArgs& a, int* err, cudaStream_t s) {
       if (a.Sk >= 1024) return launch_cfg<AttnCfg<64, 128, 2, 48, true, true>>(a, err, s);
       return launch_cfg<AttnCfg<64, 64, 4, 48, true>>(a, err, s);  // short key sets (cross-attention)
     case 64: return launch_cfg<AttnCfg<64, 64, 3, 64, false>>(a, err, s);
-    case 80: return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);  // 128-key tiles
+    case 80:  // 128-key tiles; 64-key tiles for the 77 context keys (cross-attention 6.44 -> 5.65 us on B200)
+      if (a.Sk <= 128) return launch_cfg<AttnCfg<128, 64, 1, 80, false>>(a, err, s);
+      return launch_cfg<AttnCfg<128, 128, 1, 80, false>>(a, err, s);
     case 160: return launch_cfg<AttnCfg<192, 64, 1, 160, false>>(a, err, s);
     default: return cudaErrorInvalidValue;
   }
