@@ -82,10 +82,11 @@ struct GemmDev {
   const float* wscale;       // wo8: per-output-channel weight scale [N]
   int* err;
   // LayerNorm folded into the GEMMs around it. Producer (plain single-pass epilogue): per output row,
-  // the (sum, sum of squares) of this tile's columns goes to stat_out[m * stat_ld + n_blk]. Consumer
-  // (attention-head or GEGLU epilogue): A is the raw row x, W already carries gamma; per row
-  // mean / rstd come from the stat_parts partials at stat_in[m * stat_parts ..], and the epilogue
-  // computes rstd * (acc - mean * colsum[n]) + bias[n] (bias = b + W beta).
+  // each epilogue warp's (sum, sum of squares) over its column chunks of the tile goes to
+  // stat_out[m * stat_ld + kSplit * n_blk + warp half]. Consumer (attention-head epilogue): A is the raw
+  // row x, W already carries gamma; per row mean / rstd come from the stat_parts partials at
+  // stat_in[m * stat_parts ..], and the epilogue computes rstd * (acc - mean * colsum[n]) + bias[n]
+  // (bias = b + W beta).
   float2* stat_out;
   int stat_ld;
   const float2* stat_in;
@@ -174,7 +175,7 @@ __device__ __forceinline__ void add8_f32(const float* src, float (&v)[8]) {  // 
 // Address of output element (m, n) of a plain fp16 output. For the taps == 4 upsample convolution,
 // GEMM row m is input pixel (I, j) (I = m / W counting rows of all images, j = m % W) and column n is
 // channel c of phase ph = 2 py + px (n = ph * up_co + c); it lands on output pixel (2I + py, 2j + px)
-// of the [2I', 2W] NHWC output, i.e. output row 2 m + 2 W I + 2 W py + px.
+// of the NHWC output (rows of 2W pixels, all images stacked), i.e. output row 2 m + 2 W I + 2 W py + px.
 __device__ __forceinline__ __half* out_at(const GemmDev& p, int m, int n) {
   if (p.up_w) {
     const int ph = n / p.up_co;
@@ -1144,7 +1145,7 @@ cudaError_t set_gemm_smem() {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, EK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN, W8, PAIR>::kSmem);
     if (e != cudaSuccess) return e;
-    if (EK == kEkGeneric && !PAIR) {  // cluster K splits of up to 16 CTAs
+    if (EK == kEkGeneric && !PAIR) {  // cluster K splits of up to kMaxCsplitCtas (> 8) CTAs
       e = cudaFuncSetAttribute(gemm_tc_kernel<BN, W8, PAIR, EK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return e;
     }
